@@ -1,0 +1,446 @@
+#!/usr/bin/env python
+"""Benchmark of the splatting hot path on B200.
+
+Workload (the configuration the headline metric is quoted
+on): 1,000,000 Gaussians, SH degree 3, 1920x1080, fov 50, antialias on.  One
+step = GaussianModel.render(camera) forward (fused preprocess, binning,
+compositing) + L1 loss against a U(0,1) target + backward to every raw
+parameter (means, quats, log-scales, opacity logits, sh_dc, sh_rest).
+Under torchrun with N ranks each rank renders its own view of the same
+scene (weak scaling) and the per-Gaussian gradients (59 floats each) are
+summed over ranks with one NCCL all-reduce — the data-parallel training step.
+
+Prints one JSON line (rank 0).  `value` is whole-job milliseconds per frame:
+the max-over-ranks step time divided by the frames (views) the job rendered
+per step.  `--impl reference` times the CPU oracle (a restatement of the
+reference's algorithm; mlx3D itself needs Apple's MLX/Metal) instead.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "fwd+bwd ms/frame @1080p 1M Gaussians SH3; views/s at 1/2/4/8 B200"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--config", type=int, default=2, help="scene config (2 = the headline workload)")
+    ap.add_argument("--n", type=int, default=None, help="override the Gaussian count (profiling runs)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+# --------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons every 200 ms while active."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread is not None:
+                self.thread.join(timeout=2)
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ------------------------------------------------------------ distributed glue
+def dist_setup(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        backend = "nccl" if args.impl == "ours" else "gloo"
+        if backend == "nccl":
+            torch.cuda.set_device(local)
+            dist.init_process_group("nccl", device_id=torch.device("cuda", local))
+        else:
+            dist.init_process_group("gloo")
+    elif torch.cuda.is_available() and args.impl == "ours":
+        torch.cuda.set_device(local)
+    return world, rank, local
+
+
+def view_camera(scene, rank: int):
+    """Rank r renders the scene from azimuth 30 + 45 r degrees (rank 0 is the
+    config's own camera)."""
+    from mlx3d_b200.cameras import Camera
+    from mlx3d_b200.scenes import _eye_from_angles
+
+    cfg = scene.config
+    if rank == 0:
+        return scene.cameras[0]
+    radius = float(scene.cameras[0].camera_center.norm())
+    eye = _eye_from_angles(radius, 30.0 + 45.0 * rank, 20.0)
+    return Camera.look_at(eye=eye, fov=cfg.fov, width=cfg.width, height=cfg.height)
+
+
+# ---------------------------------------------------------------- our arm
+# Algorithmic bytes per unit of each entry point ("Roofline").
+def stage_bytes(stage: str, n: int, d: int, pixels: int, sh_rest_floats: int) -> float:
+    sh = 4 * (3 + sh_rest_floats)
+    if stage == "gs_preprocess_forward":
+        return n * (12 + 16 + 12 + 4 + sh) + n * (8 + 12 + 4 + 4 + 4 + 12 + 4 + 4)
+    if stage == "gs_preprocess_backward":
+        return n * (12 + 16 + 12 + 4 + sh) + n * (8 + 12 + 12 + 4) + n * (12 + 16 + 12 + 4 + sh)
+    if stage == "gs_bin_begin":
+        # depth keys (read depth+count, write key+val), 4 radix passes over N
+        # (read key twice, value once, write key+value), scan reading counts
+        # through the permutation twice and writing offsets
+        return n * 16 + 4 * n * 20 + n * (8 + 8 + 4)
+    if stage == "gs_bin_end":
+        # duplication (read perm, offset, means2d, radius; write key+value per
+        # duplicate), two tile-sort passes over D, ranges (read keys)
+        return n * 20 + d * 8 + 2 * d * 20 + d * 4
+    if stage == "gs_rasterize_forward":
+        return d * 40 + pixels * 20
+    if stage == "gs_rasterize_backward":
+        return d * 40 + pixels * 24 + n * 36
+    return 0.0
+
+
+def run_ours(args, world, rank, local):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+
+    from mlx3d_b200 import _native as nat
+    from mlx3d_b200.scenes import make_scene
+    from mlx3d_b200.splatting import GaussianModel
+
+    dev = torch.device("cuda", local)
+    scene = make_scene(args.config, n=args.n)
+    cfg = scene.config
+    cam = view_camera(scene, rank)
+    params = scene.torch_params(device=dev, requires_grad=True)
+    model = GaussianModel(params, sh_degree=3)
+    model.active_sh_degree = cfg.sh_degree
+    target = scene.target(view=rank, device=dev)
+    plist = list(params.values())
+
+    def allreduce_grads():
+        if world > 1:
+            for p in plist:
+                dist.all_reduce(p.grad)
+
+    def step():
+        for p in plist:
+            p.grad = None
+        out = model.render(cam, antialias=cfg.antialias)
+        loss = (out["image"] - target).abs().mean()
+        loss.backward()
+        allreduce_grads()
+        return loss
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    torch.cuda.synchronize()
+    lib = nat.load()
+    launches0 = lib.gs_kernel_launch_count()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        start.record()
+        for _ in range(args.steps):
+            step()
+        end.record()
+        torch.cuda.synchronize()
+    barrier()
+    launches = lib.gs_kernel_launch_count() - launches0
+    ms_step = start.elapsed_time(end) / args.steps
+    t = torch.tensor([ms_step], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms_step = float(t.item())
+
+    # ---- per-entry-point device time (CUDA events around each library call,
+    # on the launching stream), a separate pass after the timed region.
+    stage_ms: dict[str, list[float]] = {}
+    orig_call = nat.call
+
+    def timed_call(name, *a):
+        s = torch.cuda.current_stream()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(s)
+        orig_call(name, *a)
+        e1.record(s)
+        stage_ms.setdefault(name, []).append((e0, e1))
+
+    nat.call = timed_call
+    try:
+        prof_steps = 3
+        for _ in range(prof_steps):
+            step()
+        torch.cuda.synchronize()
+    finally:
+        nat.call = orig_call
+    stages = {k: sum(a.elapsed_time(b) for a, b in v) / prof_steps for k, v in stage_ms.items()}
+    with torch.no_grad():
+        out = model.render(cam, antialias=cfg.antialias)
+        from mlx3d_b200.splatting.tiles import bin_gaussians
+
+        ids, _, _, _ = bin_gaussians(out["means2d"], out["radii"], out["depths"], cam.width, cam.height)
+        d = int(ids.shape[0])
+        visible = int((out["radii"] > 0).sum().item())
+    n = scene.params["means"].shape[0]
+    pixels = cam.width * cam.height
+    rest = scene.params["sh_rest"].shape[1] * 3
+    dom = max(stages, key=stages.get)
+    peaks = {}
+    pk = ROOT / "MEASURED_PEAKS.json"
+    if pk.exists():
+        peaks = json.loads(pk.read_text())
+    hbm_peak = peaks.get("hbm_gbs", 6650.0)
+    peak_src = "measured" if "hbm_gbs" in peaks else "fallback"
+    alg = stage_bytes(dom, n, d, pixels, rest)
+    achieved = alg / (stages[dom] * 1e-3) / 1e9
+    stage_rows = {
+        k: {"ms": round(v, 4), "alg_gb_s": round(stage_bytes(k, n, d, pixels, rest) / (v * 1e-3) / 1e9, 1)}
+        for k, v in sorted(stages.items(), key=lambda kv: -kv[1])
+    }
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        traffic = json.loads(tf.read_text()).get(dom)
+
+    # ---- end to end through the public API with host buffers
+    e2e = None
+    if not args.no_e2e:
+        host = {k: v.detach().cpu().pin_memory() for k, v in params.items()}
+        host_target = target.cpu().pin_memory()
+        loss_host = torch.empty((), dtype=torch.float32).pin_memory()
+        h2d = sum(v.numel() * 4 for v in host.values()) + host_target.numel() * 4
+
+        def e2e_step():
+            with torch.no_grad():
+                for k, p in params.items():
+                    p.copy_(host[k], non_blocking=True)
+                target.copy_(host_target, non_blocking=True)
+            loss = step()
+            loss_host.copy_(loss.detach(), non_blocking=True)
+
+        for _ in range(max(1, args.warmup // 2)):
+            e2e_step()
+        torch.cuda.synchronize()
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(args.steps):
+            e2e_step()
+        e1.record()
+        torch.cuda.synchronize()
+        te = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": round(float(te.item()) / world, 4), "unit": "ms/frame", "h2d_bytes_per_step": int(h2d),
+               "d2h_bytes_per_step": 4}
+
+    if rank != 0:
+        return None
+    clk = clocks.summary()
+    line = {
+        "metric": METRIC,
+        "value": round(ms_step / world, 4),
+        "unit": "ms/frame",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms_step, 4),
+        "views_per_s": round(1000.0 * world / ms_step, 2),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded PCG64 scene of BASELINE config %d)" % cfg.index,
+        "config": {
+            "workload": f"C{cfg.index}: {n:,} Gaussians, SH{cfg.sh_degree}, {cam.width}x{cam.height}, "
+                        f"fov {cfg.fov:g}, antialias={cfg.antialias}; GaussianModel.render + L1 + backward",
+            "gaussians": n,
+            "width": cam.width,
+            "height": cam.height,
+            "views_per_step": world,
+            "duplicates": d,
+            "visible_gaussians": visible,
+            "parallelism": f"views sharded over {world} GPU(s); per-Gaussian gradient all-reduce (NCCL)"
+                           if world > 1 else "single GPU",
+            "l2": "no flush: per-step working set (parameters %.0f MB + gradients + image buffers) exceeds the "
+                  "126 MB L2" % (sum(v.nbytes for v in scene.params.values()) / 1e6),
+        },
+        "e2e": e2e,
+        "gpu_launches": int(launches),
+        "clocks": clk,
+        "stages_ms": stage_rows,
+        "roofline": {
+            "kernel": dom,
+            "bound": "hbm",
+            "achieved": round(achieved, 1),
+            "peak": hbm_peak,
+            "unit": "GB/s",
+            "frac": round(achieved / hbm_peak, 4),
+            "peak_source": peak_src,
+            "traffic": traffic,
+            "algorithmic_bytes": alg,
+        },
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(scene, cam, cfg, steps=1)
+    return line
+
+
+# ------------------------------------------------------- CPU oracle baseline
+def _oracle_frame(scene, cam, cfg, threads=0):
+    import numpy as np
+
+    import oracle.oracle as orc
+
+    p = scene.params
+    s, o = orc.activate(p["scales"], p["opacities"])
+    sh = np.concatenate([p["sh_dc"], p["sh_rest"]], axis=1)
+    fwd = orc.render(cam.to_native(), cam.width, cam.height, p["means"], p["quats"], s, o, sh=sh,
+                     sh_degree=cfg.sh_degree, antialias=cfg.antialias, threads=threads)
+    target = scene.target(view=0, device="cpu").numpy()
+    g_img = (np.sign(fwd["image"] - target) / fwd["image"].size).astype(np.float32)
+    orc.render_grads(cam, p["means"], p["quats"], s, o, sh=sh, sh_degree=cfg.sh_degree, antialias=cfg.antialias,
+                     grad_image=g_img, threads=threads, fwd=fwd)
+    return fwd
+
+
+def cpu_baseline(scene, cam, cfg, steps=1):
+    import torch
+
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        _oracle_frame(scene, cam, cfg)
+    ms = (time.perf_counter() - t0) * 1000.0 / steps
+    return {"value": round(ms, 1), "unit": "ms/frame", "cores": cores, "kind": "port",
+            "sample": f"{steps} full frame(s) of the same workload: C++ oracle (OpenMP, {cores} threads) for "
+                      "projection, SH, binning and both compositors; torch float64 autograd (CPU) for the "
+                      "per-Gaussian backward"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return None
+    from mlx3d_b200.scenes import make_scene
+
+    scene = make_scene(args.config, n=args.n)
+    cam = scene.cameras[0]
+    cfg = scene.config
+    steps = max(1, min(args.steps, 3))
+    warm = min(args.warmup, 1)
+    for _ in range(warm):
+        _oracle_frame(scene, cam, cfg)
+    cb = cpu_baseline(scene, cam, cfg, steps=steps)
+    cb["sample"] += f"; {steps} timed step(s) of the {args.steps} requested (each a full frame), {warm} warm-up"
+    n = scene.params["means"].shape[0]
+    return {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": cb["value"],
+        "unit": "ms/frame",
+        "n_gpus": world,
+        "steps": steps,
+        "warmup": warm,
+        "ms_per_step": cb["value"],
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded PCG64 scene of BASELINE config %d)" % cfg.index,
+        "config": {"workload": f"C{cfg.index}: {n:,} Gaussians, SH{cfg.sh_degree}, {cam.width}x{cam.height}; "
+                               "render + L1 + backward on the CPU oracle (mlx3D needs Apple MLX/Metal, which "
+                               "cannot run here)"},
+        "cpu_baseline": cb,
+        "e2e": {"value": cb["value"], "unit": "ms/frame", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_setup(args)
+    if args.impl == "reference":
+        line = run_reference(args, world, rank)
+    else:
+        line = run_ours(args, world, rank, local)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    import torch.distributed as dist
+
+    if dist.is_initialized():
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

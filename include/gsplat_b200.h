@@ -1,0 +1,191 @@
+/*
+ * gsplat_b200 — C ABI of the B200-native (sm_100a) Gaussian-splatting
+ * rasterizer path of mlx3D.
+ *
+ * The reference (mlx3D 0.2.0) has no native FFI: its device seam is
+ * `mx.fast.metal_kernel(...)` wrapped by `@mx.custom_function` with a `.vjp`
+ * (src/mlx3d/splatting/rasterize.py:292-403), and the elementwise MLX graphs of
+ * projection.py / sh.py / tiles.py.  Each entry point below replaces one of
+ * those seams; the comment above it names the reference code it stands for.
+ *
+ * Conventions
+ *  - Plain device pointers (float32 / int32, C-contiguous) and sizes.  The
+ *    library never allocates or frees caller memory; binning scratch is a
+ *    caller-provided workspace sized by the *_workspace_*_bytes queries.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  All calls are
+ *    asynchronous on that stream; nothing synchronises the host.
+ *  - Return value: GS_OK or a GS_ERR_* code; gs_last_error() returns a
+ *    human-readable message for the last failing call on the calling thread.
+ *  - Optional pointers may be NULL where marked.
+ */
+#ifndef GSPLAT_B200_H
+#define GSPLAT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define GS_OK 0
+#define GS_ERR_INVALID_ARG 1
+#define GS_ERR_CUDA 2
+#define GS_ERR_CAPACITY 3
+
+/* Activation flags for gs_preprocess_forward/backward
+ * (src/mlx3d/splatting/model.py:116-122): scales given as log-scales,
+ * opacities given as logits. */
+#define GS_ACT_EXP_SCALES 1
+#define GS_ACT_SIGMOID_OPACITY 2
+
+/* Pinhole camera as the projection sees it (src/mlx3d/cameras/cameras.py:139-173).
+ * The reference mixes Python doubles with float32 arrays; each field below is
+ * the float32 value the reference's expression ends up using:
+ *   fx..cy      = float(camera.fx) ...
+ *   neg_fx      = float(-camera.fx)                 (projection.py:83)
+ *   clip_x      = float(1.3 * (0.5 * width / fx))   (projection.py:70-72)
+ *   znear       = float(camera.znear)               (projection.py:136)
+ *   center      = camera_center = -R^T t            (cameras.py:270-273)  */
+typedef struct gs_camera {
+  float R[9]; /* row-major world->camera rotation */
+  float t[3];
+  float fx, fy, cx, cy;
+  float neg_fx, neg_fy;
+  float clip_x, clip_y;
+  float znear;
+  float center[3];
+  int32_t width, height;
+} gs_camera;
+
+/* Library version (major*10000 + minor*100 + patch). */
+int gs_version(void);
+
+/* Message of the last failing call on this thread ("" if none). */
+const char* gs_last_error(void);
+
+/* Number of kernels this library has launched in this process (all
+ * devices, all threads); for launch accounting in benchmarks. */
+uint64_t gs_kernel_launch_count(void);
+
+/* ---------------------------------------------------------------- projection
+ * project_gaussians: EWA projection of (N,3) means, (N,4) wxyz quats and (N,3)
+ * linear scales to means2d (N,2), conics (N,3), depths (N), radii (N, float,
+ * 0 = culled) and compensation (N).  Replaces src/mlx3d/splatting/projection.py:24-146. */
+int gs_project_forward(const gs_camera* cam, const float* means, const float* quats,
+                       const float* scales, int64_t n, float blur, int antialias,
+                       float* means2d, float* conics, float* depths, float* radii,
+                       float* compensation, void* stream);
+
+/* Vector-Jacobian product of gs_project_forward (what MLX autodiff computes
+ * through projection.py:56-146).  Any cotangent may be NULL (= zero).  Writes
+ * (overwrites) g_means (N,3), g_quats (N,4), g_scales (N,3). */
+int gs_project_backward(const gs_camera* cam, const float* means, const float* quats,
+                        const float* scales, int64_t n, float blur, int antialias,
+                        const float* g_means2d, const float* g_conics, const float* g_depths,
+                        const float* g_compensation, float* g_means, float* g_quats,
+                        float* g_scales, void* stream);
+
+/* ------------------------------------------------------------------------ SH
+ * eval_sh(degree, sh (N,K,C), dirs (N,3)) -> (N,C), offset by +0.5, unclamped.
+ * Replaces src/mlx3d/splatting/sh.py:41-78.  K >= (degree+1)^2. */
+int gs_eval_sh_forward(int degree, const float* sh, int64_t n, int k, int channels,
+                       const float* dirs, float* out, void* stream);
+
+/* VJP of gs_eval_sh_forward: g_sh (N,K,C) (entries beyond (degree+1)^2 are
+ * written as 0) and, if g_dirs != NULL, g_dirs (N,3). */
+int gs_eval_sh_backward(int degree, const float* sh, int64_t n, int k, int channels,
+                        const float* dirs, const float* g_out, float* g_sh, float* g_dirs,
+                        void* stream);
+
+/* ------------------------------------------------------ fused per-Gaussian pass
+ * The per-Gaussian half of render_gaussians (src/mlx3d/splatting/render.py:56-80
+ * plus tiles.py:54-65) in one kernel: projection, opacity * compensation,
+ * view-dependent SH colour max(eval_sh(...), 0) with stop-gradient directions,
+ * and the per-Gaussian tile count ("tiles touched").
+ *   sh_dc   : (N, 3) rows with stride sh_dc_stride floats   (NULL: no colour)
+ *   sh_rest : (N, K-1, 3) rows with stride sh_rest_stride   (NULL if degree 0)
+ *   flags   : GS_ACT_* activations applied to scales / opacities first.
+ * Outputs: means2d (N,2), conics (N,3), depths, radii, compensation (N),
+ * colors (N,3) (ignored if sh_dc == NULL), opacities_out (N), tiles_touched (N). */
+int gs_preprocess_forward(const gs_camera* cam, const float* means, const float* quats,
+                          const float* scales, const float* opacities, const float* sh_dc,
+                          int64_t sh_dc_stride, const float* sh_rest, int64_t sh_rest_stride,
+                          int sh_degree, int64_t n, float blur, int antialias, int flags,
+                          float* means2d, float* conics, float* depths, float* radii,
+                          float* compensation, float* colors, float* opacities_out,
+                          int32_t* tiles_touched, void* stream);
+
+/* VJP of gs_preprocess_forward.  Cotangents g_means2d (N,2), g_conics (N,3),
+ * g_colors (N,3), g_opacities_out (N) come from gs_rasterize_backward;
+ * g_depths / g_compensation (N) may be NULL.  Writes g_means (N,3),
+ * g_quats (N,4), g_scales (N,3), g_opacities (N) with respect to the raw
+ * inputs (after the activations in `flags`), and the SH gradient rows
+ * g_sh_dc / g_sh_rest with the same strides as the inputs. */
+int gs_preprocess_backward(const gs_camera* cam, const float* means, const float* quats,
+                           const float* scales, const float* opacities, const float* sh_dc,
+                           int64_t sh_dc_stride, const float* sh_rest, int64_t sh_rest_stride,
+                           int sh_degree, int64_t n, float blur, int antialias, int flags,
+                           const float* g_means2d, const float* g_conics,
+                           const float* g_colors, const float* g_opacities_out,
+                           const float* g_depths, const float* g_compensation,
+                           float* g_means, float* g_quats, float* g_scales,
+                           float* g_opacities, float* g_sh_dc, float* g_sh_rest,
+                           void* stream);
+
+/* ------------------------------------------------------------------- binning
+ * bin_gaussians (src/mlx3d/splatting/tiles.py:19-182), split where the
+ * reference itself synchronises with the host (tiles.py:68):
+ *   1. gs_tile_counts     tiles touched per Gaussian          (tiles.py:49-65)
+ *   2. gs_bin_begin       stable depth order of the touching Gaussians and the
+ *                         duplicate total D, written to *d_total on the device
+ *                                                             (tiles.py:67-68,167-168)
+ *   3. (host reads D, sizes the D-dependent buffers)
+ *   4. gs_bin_end         duplicates, stable sort by tile, tile ranges
+ *                                                             (tiles.py:77-89,169-182)
+ * The result equals the reference's key order tile*N + rank(depth): ties in
+ * depth keep Gaussian index order.  Empty tiles get the range [0, 0). */
+int gs_tile_counts(const float* means2d, const float* radii, int64_t n, int width, int height,
+                   int32_t* tiles_touched, void* stream);
+
+size_t gs_bin_workspace_n_bytes(int64_t n);
+size_t gs_bin_workspace_d_bytes(int64_t d);
+
+int gs_bin_begin(const float* depths, const int32_t* tiles_touched, int64_t n, void* ws_n,
+                 size_t ws_n_bytes, int64_t* d_total, void* stream);
+
+int gs_bin_end(const float* means2d, const float* radii, int64_t n, int64_t d, int width,
+               int height, void* ws_n, size_t ws_n_bytes, void* ws_d, size_t ws_d_bytes,
+               int32_t* sorted_ids, int32_t* tile_ranges, void* stream);
+
+/* --------------------------------------------------------------- compositing
+ * Forward tile compositor (gs_rasterize_forward Metal kernel,
+ * src/mlx3d/splatting/rasterize.py:28-98, 345-361, and the depth kernel
+ * :223-290).  `channels` colour/feature channels per Gaussian (0..64,
+ * colors (N,channels)); background (channels) may be NULL (= 0).
+ * Outputs (each may be NULL except final_T): image (H,W,channels),
+ * final_T (H,W), n_contrib (H,W) int32, depth (H,W) (needs `depths`). */
+int gs_rasterize_forward(const float* means2d, const float* conics, const float* colors,
+                         int channels, const float* opacities, const float* depths,
+                         const int32_t* sorted_ids, const int32_t* tile_ranges,
+                         const float* background, int width, int height, int tiles_x,
+                         int tiles_y, float* image, float* final_T, int32_t* n_contrib,
+                         float* depth, void* stream);
+
+/* Backward tile compositor (gs_rasterize_backward, rasterize.py:100-221,
+ * 364-403).  grad_final_T may be NULL.  Zeroes, then accumulates
+ * grad_means2d (N,2), grad_conics (N,3), grad_colors (N,channels),
+ * grad_opacities (N). */
+int gs_rasterize_backward(const float* means2d, const float* conics, const float* colors,
+                          int channels, const float* opacities, int64_t n,
+                          const int32_t* sorted_ids, const int32_t* tile_ranges,
+                          const float* background, int width, int height, int tiles_x,
+                          int tiles_y, const float* final_T, const int32_t* n_contrib,
+                          const float* grad_image, const float* grad_final_T,
+                          float* grad_means2d, float* grad_conics, float* grad_colors,
+                          float* grad_opacities, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* GSPLAT_B200_H */

@@ -1,0 +1,145 @@
+"""ctypes binding of the sm_100a C-ABI library ``_lib/libgsplat_b200.so``.
+
+Every product entry point of this package goes through this module; there is
+no CPU or PyTorch fallback.  Loading fails loudly when the library has not
+been built (``python -m mlx3d_b200.build``), and every call checks that its
+tensors are CUDA float32 / int32 and contiguous.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_float, c_int, c_int32, c_int64, c_size_t, c_void_p, c_char_p
+from pathlib import Path
+
+import torch
+
+LIB_PATH = Path(__file__).resolve().parent / "_lib" / "libgsplat_b200.so"
+
+GS_OK = 0
+GS_ERR_INVALID_ARG = 1
+GS_ERR_CUDA = 2
+GS_ERR_CAPACITY = 3
+
+GS_ACT_EXP_SCALES = 1
+GS_ACT_SIGMOID_OPACITY = 2
+
+
+class GsCamera(ctypes.Structure):
+    """Mirror of ``gs_camera`` in include/gsplat_b200.h."""
+
+    _fields_ = [
+        ("R", c_float * 9),
+        ("t", c_float * 3),
+        ("fx", c_float),
+        ("fy", c_float),
+        ("cx", c_float),
+        ("cy", c_float),
+        ("neg_fx", c_float),
+        ("neg_fy", c_float),
+        ("clip_x", c_float),
+        ("clip_y", c_float),
+        ("znear", c_float),
+        ("center", c_float * 3),
+        ("width", c_int32),
+        ("height", c_int32),
+    ]
+
+
+# name -> (restype, argtypes)
+_P = c_void_p
+_SIGS = {
+    "gs_version": (c_int, []),
+    "gs_last_error": (c_char_p, []),
+    "gs_kernel_launch_count": (ctypes.c_uint64, []),
+    "gs_project_forward": (c_int, [POINTER(GsCamera), _P, _P, _P, c_int64, c_float, c_int, _P, _P, _P, _P, _P, _P]),
+    "gs_project_backward": (
+        c_int,
+        [POINTER(GsCamera), _P, _P, _P, c_int64, c_float, c_int, _P, _P, _P, _P, _P, _P, _P, _P],
+    ),
+    "gs_eval_sh_forward": (c_int, [c_int, _P, c_int64, c_int, c_int, _P, _P, _P]),
+    "gs_eval_sh_backward": (c_int, [c_int, _P, c_int64, c_int, c_int, _P, _P, _P, _P, _P]),
+    "gs_preprocess_forward": (
+        c_int,
+        [POINTER(GsCamera), _P, _P, _P, _P, _P, c_int64, _P, c_int64, c_int, c_int64, c_float, c_int, c_int]
+        + [_P] * 8
+        + [_P],
+    ),
+    "gs_preprocess_backward": (
+        c_int,
+        [POINTER(GsCamera), _P, _P, _P, _P, _P, c_int64, _P, c_int64, c_int, c_int64, c_float, c_int, c_int]
+        + [_P] * 6
+        + [_P] * 6
+        + [_P],
+    ),
+    "gs_tile_counts": (c_int, [_P, _P, c_int64, c_int, c_int, _P, _P]),
+    "gs_bin_workspace_n_bytes": (c_size_t, [c_int64]),
+    "gs_bin_workspace_d_bytes": (c_size_t, [c_int64]),
+    "gs_bin_begin": (c_int, [_P, _P, c_int64, _P, c_size_t, _P, _P]),
+    "gs_bin_end": (c_int, [_P, _P, c_int64, c_int64, c_int, c_int, _P, c_size_t, _P, c_size_t, _P, _P, _P]),
+    "gs_rasterize_forward": (
+        c_int,
+        [_P, _P, _P, c_int, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P],
+    ),
+    "gs_rasterize_backward": (
+        c_int,
+        [_P, _P, _P, c_int, _P, c_int64, _P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P, _P, _P, _P, _P],
+    ),
+}
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (once) and return the library; raises if it is missing."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise ImportError(
+            f"mlx3d_b200: CUDA library not built ({LIB_PATH}); run `python -m mlx3d_b200.build`"
+        )
+    lib = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in _SIGS.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+def exported_symbols() -> list[str]:
+    return list(_SIGS)
+
+
+def call(name: str, *args) -> None:
+    """Call ``name`` and raise on a non-zero status (ValueError for bad
+    arguments, RuntimeError otherwise)."""
+    lib = load()
+    status = getattr(lib, name)(*args)
+    if status != GS_OK:
+        msg = (lib.gs_last_error() or b"").decode(errors="replace")
+        if status == GS_ERR_INVALID_ARG:
+            raise ValueError(f"{name}: {msg}")
+        raise RuntimeError(f"{name} failed (status {status}): {msg}")
+
+
+def ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def require_cuda(name: str, t: torch.Tensor, dtype=torch.float32) -> torch.Tensor:
+    """Return ``t`` as a contiguous CUDA tensor of ``dtype`` (converting the
+    dtype like the reference's ``astype(mx.float32)``); CPU tensors are an
+    error: this package has no CPU path."""
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.device.type != "cuda":
+        raise ValueError(f"{name} must be a CUDA tensor (got device {t.device}); mlx3d_b200 has no CPU path")
+    if t.dtype != dtype:
+        t = t.to(dtype)
+    return t.contiguous()

@@ -1,0 +1,36 @@
+// Error reporting and version entry points of the C ABI.
+#include <stdarg.h>
+
+#include <atomic>
+
+#include "gs_common.cuh"
+
+namespace gs {
+
+static thread_local char g_last_error[512] = "";
+
+int set_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_last_error, sizeof(g_last_error), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+void clear_error() { g_last_error[0] = '\0'; }
+
+static std::atomic<unsigned long long> g_launches{0};
+
+void note_launches(int n) { g_launches.fetch_add((unsigned long long)n, std::memory_order_relaxed); }
+
+}  // namespace gs
+
+extern "C" {
+
+int gs_version(void) { return 100; }  // 0.1.0
+
+const char* gs_last_error(void) { return gs::g_last_error; }
+
+uint64_t gs_kernel_launch_count(void) { return gs::g_launches.load(std::memory_order_relaxed); }
+
+}  // extern "C"

@@ -1,0 +1,403 @@
+// CPU ORACLE — TEST INFRASTRUCTURE ONLY.
+//
+// A plain C++ restatement of mlx3D's Gaussian-splatting path, used by tests/,
+// __graft_entry__.smoke() and bench.py's cpu_baseline / --impl reference arm
+// as the checker and CPU baseline.  Product code never calls it.
+//
+// Each function follows the reference file:line named in its comment, in the
+// reference's order of float32 operations.  Exactly rounded float32 primitives
+// and the exponential come from mlx3d_b200/csrc/gs_math.h (the reference's
+// MLX / Metal exp is not reproducible off Apple hardware; both this oracle and
+// the CUDA kernels use the same published-method exp so cut-off decisions
+// agree bit for bit).  Build: oracle/Makefile (-O2 -ffp-contract=off, OpenMP).
+//
+// Parity pinning: MLX cannot run in this environment (macOS arm64 wheels
+// only), so the oracle is pinned by the known-answer tests of the reference's
+// own test suite (tests/test_splatting.py:57-72, 114-195, 198-211) and by the
+// naive O(N*H*W) renderer of src/mlx3d/splatting/reference.py restated in
+// tests/oracle_torch.py; see tests/test_oracle.py.
+#include <algorithm>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <numeric>
+#include <vector>
+
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+#include "../include/gsplat_b200.h"
+#include "../mlx3d_b200/csrc/gs_math.h"
+
+namespace {
+
+constexpr int TILE = 16;
+constexpr int BLOCK = 256;
+
+// projection.py:56-138, one Gaussian.
+void project_one(const gs_camera& cam, const float* m, const float* qr, const float* s, float blur,
+                 bool aa, float* out_uv, float* out_conic, float* out_z, float* out_r,
+                 float* out_comp) {
+  const float* R = cam.R;
+  const float x = gs_add(gs_add(gs_add(gs_mul(m[0], R[0]), gs_mul(m[1], R[1])), gs_mul(m[2], R[2])), cam.t[0]);
+  const float y = gs_add(gs_add(gs_add(gs_mul(m[0], R[3]), gs_mul(m[1], R[4])), gs_mul(m[2], R[5])), cam.t[1]);
+  const float z = gs_add(gs_add(gs_add(gs_mul(m[0], R[6]), gs_mul(m[1], R[7])), gs_mul(m[2], R[8])), cam.t[2]);
+  const float z_safe = gs_maxf(z, 1e-6f);  // :61
+  out_uv[0] = gs_add(gs_div(gs_mul(cam.fx, x), z_safe), cam.cx);  // :64
+  out_uv[1] = gs_add(gs_div(gs_mul(cam.fy, y), z_safe), cam.cy);  // :65
+  // clip(v, lo, hi) = minimum(maximum(v, lo), hi)  (:72-73)
+  const float tx = gs_mul(gs_minf(gs_maxf(gs_div(x, z_safe), -cam.clip_x), cam.clip_x), z_safe);
+  const float ty = gs_mul(gs_minf(gs_maxf(gs_div(y, z_safe), -cam.clip_y), cam.clip_y), z_safe);
+  const float inv_z = gs_div(1.0f, z_safe);
+  const float inv_z2 = gs_mul(inv_z, inv_z);
+  const float j00 = gs_mul(cam.fx, inv_z);
+  const float j02 = gs_mul(gs_mul(cam.neg_fx, tx), inv_z2);
+  const float j11 = gs_mul(cam.fy, inv_z);
+  const float j12 = gs_mul(gs_mul(cam.neg_fy, ty), inv_z2);
+  float T[2][3];
+  for (int k = 0; k < 3; ++k) {  // :87-92
+    T[0][k] = gs_add(gs_mul(j00, R[k]), gs_mul(j02, R[6 + k]));
+    T[1][k] = gs_add(gs_mul(j11, R[3 + k]), gs_mul(j12, R[6 + k]));
+  }
+  const float nrm = gs_sqrt(gs_add(gs_add(gs_add(gs_mul(qr[0], qr[0]), gs_mul(qr[1], qr[1])), gs_mul(qr[2], qr[2])), gs_mul(qr[3], qr[3])));
+  const float qw = gs_div(qr[0], nrm), qx = gs_div(qr[1], nrm), qy = gs_div(qr[2], nrm), qz = gs_div(qr[3], nrm);
+  float Q[3][3];  // :97-105
+  Q[0][0] = gs_sub(1.0f, gs_mul(2.0f, gs_add(gs_mul(qy, qy), gs_mul(qz, qz))));
+  Q[0][1] = gs_mul(2.0f, gs_sub(gs_mul(qx, qy), gs_mul(qw, qz)));
+  Q[0][2] = gs_mul(2.0f, gs_add(gs_mul(qx, qz), gs_mul(qw, qy)));
+  Q[1][0] = gs_mul(2.0f, gs_add(gs_mul(qx, qy), gs_mul(qw, qz)));
+  Q[1][1] = gs_sub(1.0f, gs_mul(2.0f, gs_add(gs_mul(qx, qx), gs_mul(qz, qz))));
+  Q[1][2] = gs_mul(2.0f, gs_sub(gs_mul(qy, qz), gs_mul(qw, qx)));
+  Q[2][0] = gs_mul(2.0f, gs_sub(gs_mul(qx, qz), gs_mul(qw, qy)));
+  Q[2][1] = gs_mul(2.0f, gs_add(gs_mul(qy, qz), gs_mul(qw, qx)));
+  Q[2][2] = gs_sub(1.0f, gs_mul(2.0f, gs_add(gs_mul(qx, qx), gs_mul(qy, qy))));
+  float M[2][3];  // :108-113
+  for (int r = 0; r < 2; ++r)
+    for (int k = 0; k < 3; ++k)
+      M[r][k] = gs_mul(gs_add(gs_add(gs_mul(T[r][0], Q[0][k]), gs_mul(T[r][1], Q[1][k])), gs_mul(T[r][2], Q[2][k])), s[k]);
+  const float a0 = gs_add(gs_add(gs_mul(M[0][0], M[0][0]), gs_mul(M[0][1], M[0][1])), gs_mul(M[0][2], M[0][2]));
+  const float b = gs_add(gs_add(gs_mul(M[0][0], M[1][0]), gs_mul(M[0][1], M[1][1])), gs_mul(M[0][2], M[1][2]));
+  const float c0 = gs_add(gs_add(gs_mul(M[1][0], M[1][0]), gs_mul(M[1][1], M[1][1])), gs_mul(M[1][2], M[1][2]));
+  const float a = gs_add(a0, blur), c = gs_add(c0, blur);  // :119-120
+  const float det = gs_sub(gs_mul(a, c), gs_mul(b, b));
+  const float det_safe = gs_maxf(det, 1e-12f);
+  out_conic[0] = gs_div(c, det_safe);
+  out_conic[1] = gs_div(-b, det_safe);
+  out_conic[2] = gs_div(a, det_safe);
+  float comp = 1.0f;
+  if (aa && blur > 0.0f) comp = gs_sqrt(gs_div(gs_maxf(gs_sub(gs_mul(a0, c0), gs_mul(b, b)), 0.0f), det_safe));
+  const float mid = gs_mul(0.5f, gs_add(a, c));  // :132-134
+  const float lam1 = gs_add(mid, gs_sqrt(gs_maxf(gs_sub(gs_mul(mid, mid), det), 0.01f)));
+  const float radius = std::ceil(gs_mul(3.0f, gs_sqrt(gs_maxf(lam1, 0.0f))));
+  const bool valid = (z > cam.znear) && (det > 0.0f);  // :136-138
+  *out_z = z;
+  *out_r = valid ? radius : 0.0f;
+  *out_comp = valid ? comp : 0.0f;
+}
+
+const float kC0 = (float)0.28209479177387814, kC1 = (float)0.4886025119029199;
+const float kC2[5] = {(float)1.0925484305920792, (float)-1.0925484305920792, (float)0.31539156525252005,
+                      (float)-1.0925484305920792, (float)0.5462742152960396};
+const float kC3[7] = {(float)-0.5900435899266435, (float)2.890611442640554, (float)-0.4570457994644658,
+                      (float)0.3731763325901154, (float)-0.4570457994644658, (float)1.445305721320277,
+                      (float)-0.5900435899266435};
+
+// sh.py:57-78, one (Gaussian, channel); sh[k * stride] is coefficient k.
+float eval_sh_one(int degree, const float* sh, int stride, float x, float y, float z) {
+  float r = gs_mul(kC0, sh[0]);
+  if (degree > 0) {
+    r = gs_sub(r, gs_mul(gs_mul(kC1, y), sh[1 * stride]));
+    r = gs_add(r, gs_mul(gs_mul(kC1, z), sh[2 * stride]));
+    r = gs_sub(r, gs_mul(gs_mul(kC1, x), sh[3 * stride]));
+    if (degree > 1) {
+      const float xx = gs_mul(x, x), yy = gs_mul(y, y), zz = gs_mul(z, z);
+      const float xy = gs_mul(x, y), yz = gs_mul(y, z), xz = gs_mul(x, z);
+      r = gs_add(r, gs_mul(gs_mul(kC2[0], xy), sh[4 * stride]));
+      r = gs_add(r, gs_mul(gs_mul(kC2[1], yz), sh[5 * stride]));
+      r = gs_add(r, gs_mul(gs_mul(kC2[2], gs_sub(gs_sub(gs_mul(2.0f, zz), xx), yy)), sh[6 * stride]));
+      r = gs_add(r, gs_mul(gs_mul(kC2[3], xz), sh[7 * stride]));
+      r = gs_add(r, gs_mul(gs_mul(kC2[4], gs_sub(xx, yy)), sh[8 * stride]));
+      if (degree > 2) {
+        r = gs_add(r, gs_mul(gs_mul(gs_mul(kC3[0], y), gs_sub(gs_mul(3.0f, xx), yy)), sh[9 * stride]));
+        r = gs_add(r, gs_mul(gs_mul(gs_mul(kC3[1], xy), z), sh[10 * stride]));
+        r = gs_add(r, gs_mul(gs_mul(gs_mul(kC3[2], y), gs_sub(gs_sub(gs_mul(4.0f, zz), xx), yy)), sh[11 * stride]));
+        r = gs_add(r, gs_mul(gs_mul(gs_mul(kC3[3], z), gs_sub(gs_sub(gs_mul(2.0f, zz), gs_mul(3.0f, xx)), gs_mul(3.0f, yy))), sh[12 * stride]));
+        r = gs_add(r, gs_mul(gs_mul(gs_mul(kC3[4], x), gs_sub(gs_sub(gs_mul(4.0f, zz), xx), yy)), sh[13 * stride]));
+        r = gs_add(r, gs_mul(gs_mul(gs_mul(kC3[5], z), gs_sub(xx, yy)), sh[14 * stride]));
+        r = gs_add(r, gs_mul(gs_mul(gs_mul(kC3[6], x), gs_sub(xx, gs_mul(3.0f, yy))), sh[15 * stride]));
+      }
+    }
+  }
+  return gs_add(r, 0.5f);
+}
+
+// tiles.py:54-65: inclusive tile bbox and count of one Gaussian.
+int tile_bbox(float x, float y, float r, int W, int H, int tx, int ty, int* bb) {
+  auto cl = [](float v, float hi) { return (int)gs_minf(gs_maxf(v, 0.0f), hi); };
+  bb[0] = cl(std::floor(gs_div(gs_sub(x, r), (float)TILE)), (float)(tx - 1));
+  bb[1] = cl(std::floor(gs_div(gs_add(x, r), (float)TILE)), (float)(tx - 1));
+  bb[2] = cl(std::floor(gs_div(gs_sub(y, r), (float)TILE)), (float)(ty - 1));
+  bb[3] = cl(std::floor(gs_div(gs_add(y, r), (float)TILE)), (float)(ty - 1));
+  const bool on = (r > 0.0f) && (gs_add(x, r) >= 0.0f) && (gs_sub(x, r) < (float)W) &&
+                  (gs_add(y, r) >= 0.0f) && (gs_sub(y, r) < (float)H);
+  return on ? (bb[1] - bb[0] + 1) * (bb[3] - bb[2] + 1) : 0;
+}
+
+int n_threads(int requested) {
+#ifdef _OPENMP
+  return requested > 0 ? requested : omp_get_max_threads();
+#else
+  (void)requested;
+  return 1;
+#endif
+}
+
+}  // namespace
+
+extern "C" {
+
+// project_gaussians (projection.py:24-146).
+void or_project(const gs_camera* cam, const float* means, const float* quats, const float* scales,
+                int64_t n, float blur, int aa, float* means2d, float* conics, float* depths,
+                float* radii, float* comp, int threads) {
+#pragma omp parallel for schedule(static) num_threads(n_threads(threads))
+  for (int64_t i = 0; i < n; ++i)
+    project_one(*cam, means + 3 * i, quats + 4 * i, scales + 3 * i, blur, aa != 0, means2d + 2 * i,
+                conics + 3 * i, depths + i, radii + i, comp + i);
+}
+
+// eval_sh (sh.py:41-78) for sh (N, K, C) and dirs (N, 3).
+void or_eval_sh(int degree, const float* sh, int64_t n, int K, int C, const float* dirs, float* out) {
+  for (int64_t i = 0; i < n; ++i)
+    for (int ch = 0; ch < C; ++ch)
+      out[i * C + ch] = eval_sh_one(degree, sh + i * K * C + ch, C, dirs[3 * i], dirs[3 * i + 1], dirs[3 * i + 2]);
+}
+
+// The SH colour step of render_gaussians (render.py:77-80): normalised view
+// directions and max(eval_sh(...), 0) for sh (N, K, 3).
+void or_sh_colors(const gs_camera* cam, int degree, const float* means, const float* sh, int64_t n,
+                  int K, float* colors, int threads) {
+#pragma omp parallel for schedule(static) num_threads(n_threads(threads))
+  for (int64_t i = 0; i < n; ++i) {
+    const float dx = gs_sub(means[3 * i], cam->center[0]);
+    const float dy = gs_sub(means[3 * i + 1], cam->center[1]);
+    const float dz = gs_sub(means[3 * i + 2], cam->center[2]);
+    const float nr = gs_maxf(gs_sqrt(gs_add(gs_add(gs_mul(dx, dx), gs_mul(dy, dy)), gs_mul(dz, dz))), 1e-8f);
+    const float x = gs_div(dx, nr), y = gs_div(dy, nr), z = gs_div(dz, nr);
+    for (int ch = 0; ch < 3; ++ch)
+      colors[3 * i + ch] = gs_maxf(eval_sh_one(degree, sh + i * K * 3 + ch, 3, x, y, z), 0.0f);
+  }
+}
+
+// Activations of GaussianModel (model.py:116-122) with the shared exp.
+void or_activate(const float* log_scales, const float* logits, int64_t n, float* scales, float* opac) {
+  for (int64_t i = 0; i < 3 * n; ++i) scales[i] = gs_expf(log_scales[i]);
+  for (int64_t i = 0; i < n; ++i) opac[i] = gs_sigmoidf(logits[i]);
+}
+
+// tiles.py:49-68: tiles touched per Gaussian; returns the duplicate total D.
+int64_t or_bin_count(const float* means2d, const float* radii, int64_t n, int W, int H, int32_t* counts) {
+  const int tx = (W + TILE - 1) / TILE, ty = (H + TILE - 1) / TILE;
+  int64_t total = 0;
+  int bb[4];
+  for (int64_t i = 0; i < n; ++i) {
+    counts[i] = tile_bbox(means2d[2 * i], means2d[2 * i + 1], radii[i], W, H, tx, ty, bb);
+    total += counts[i];
+  }
+  return total;
+}
+
+// tiles.py:77-182: duplicates in Gaussian order, key = tile * N + rank(depth)
+// with rank from a stable argsort of all depths, stable argsort of the keys,
+// per-tile [start, end) ranges with empty tiles at [0, 0).
+void or_bin_fill(const float* means2d, const float* radii, const float* depths, int64_t n, int W,
+                 int H, int64_t D, int32_t* sorted_ids, int32_t* ranges) {
+  const int tx = (W + TILE - 1) / TILE, ty = (H + TILE - 1) / TILE;
+  const int64_t num_tiles = (int64_t)tx * ty;
+  std::vector<int32_t> gid, tid;
+  gid.reserve(D);
+  tid.reserve(D);
+  int bb[4];
+  for (int64_t i = 0; i < n; ++i) {
+    const int c = tile_bbox(means2d[2 * i], means2d[2 * i + 1], radii[i], W, H, tx, ty, bb);
+    if (!c) continue;
+    const int w = bb[1] - bb[0] + 1;
+    for (int l = 0; l < c; ++l) {  // :85-89
+      gid.push_back((int32_t)i);
+      tid.push_back((bb[2] + l / w) * tx + bb[0] + l % w);
+    }
+  }
+  std::vector<int64_t> order(n);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int64_t p, int64_t q) { return depths[p] < depths[q]; });
+  std::vector<int64_t> rank(n);
+  for (int64_t r = 0; r < n; ++r) rank[order[r]] = r;
+  std::vector<int64_t> key(D);
+  for (int64_t j = 0; j < D; ++j) key[j] = (int64_t)tid[j] * n + rank[gid[j]];
+  std::vector<int64_t> idx(D);
+  std::iota(idx.begin(), idx.end(), 0);
+  std::stable_sort(idx.begin(), idx.end(), [&](int64_t p, int64_t q) { return key[p] < key[q]; });
+  std::vector<int32_t> starts(num_tiles, (int32_t)D), ends(num_tiles, 0);
+  for (int64_t p = 0; p < D; ++p) {
+    sorted_ids[p] = gid[idx[p]];
+    const int32_t t = tid[idx[p]];
+    starts[t] = std::min(starts[t], (int32_t)p);
+    ends[t] = std::max(ends[t], (int32_t)(p + 1));
+  }
+  for (int64_t t = 0; t < num_tiles; ++t) {
+    ranges[2 * t] = std::min(starts[t], ends[t]);
+    ranges[2 * t + 1] = ends[t];
+  }
+}
+
+// gs_rasterize_forward + gs_rasterize_depth (rasterize.py:28-98, 223-290) for
+// C channels (C == 0: depth only); colors (N, C).
+void or_rasterize_fwd(const float* means2d, const float* conics, const float* colors, int C,
+                      const float* opac, const float* depths, const int32_t* ids,
+                      const int32_t* ranges, const float* bg, int W, int H, float* image,
+                      float* final_T, int32_t* n_contrib, float* depth, int threads) {
+  const int tx = (W + TILE - 1) / TILE, ty = (H + TILE - 1) / TILE;
+#pragma omp parallel for schedule(dynamic, 4) num_threads(n_threads(threads))
+  for (int tile = 0; tile < tx * ty; ++tile) {
+    const int start = ranges[2 * tile], end = ranges[2 * tile + 1];
+    std::vector<float> acc(C > 0 ? C : 1);
+    for (int ly = 0; ly < TILE; ++ly)
+      for (int lx = 0; lx < TILE; ++lx) {
+        const int px = (tile % tx) * TILE + lx, py = (tile / tx) * TILE + ly;
+        if (px >= W || py >= H) continue;
+        const float pxf = (float)px + 0.5f, pyf = (float)py + 0.5f;
+        float T = 1.0f, dacc = 0.0f;
+        std::fill(acc.begin(), acc.end(), 0.0f);
+        int last = 0;
+        for (int k = start; k < end; ++k) {
+          const int g = ids[k];
+          const float dx = gs_sub(means2d[2 * g], pxf), dy = gs_sub(means2d[2 * g + 1], pyf);
+          const float* co = conics + 3 * g;
+          const float power = gs_sub(gs_mul(-0.5f, gs_add(gs_mul(gs_mul(co[0], dx), dx), gs_mul(gs_mul(co[2], dy), dy))),
+                                     gs_mul(gs_mul(co[1], dx), dy));
+          if (power > 0.0f) continue;
+          const float alpha = gs_minf(0.99f, gs_mul(opac[g], gs_expf(power)));
+          if (alpha < 1.0f / 255.0f) continue;
+          const float next_T = gs_mul(T, gs_sub(1.0f, alpha));
+          if (next_T < 1e-4f) break;
+          const float w = gs_mul(alpha, T);
+          for (int ch = 0; ch < C; ++ch) acc[ch] = gs_add(acc[ch], gs_mul(colors[(int64_t)g * C + ch], w));
+          if (depth) dacc = gs_add(dacc, gs_mul(depths[g], w));
+          T = next_T;
+          last = k - start + 1;
+        }
+        const int64_t pid = (int64_t)py * W + px;
+        for (int ch = 0; ch < C; ++ch) image[pid * C + ch] = gs_add(acc[ch], gs_mul(T, bg ? bg[ch] : 0.0f));
+        final_T[pid] = T;
+        if (n_contrib) n_contrib[pid] = last;
+        if (depth) {
+          const float al = gs_sub(1.0f, T);
+          depth[pid] = al > 1e-6f ? gs_div(dacc, al) : 0.0f;
+        }
+      }
+  }
+}
+
+// gs_rasterize_backward (rasterize.py:100-221) for C channels; sequential
+// per-pixel back-to-front replay, gradients summed per thread then reduced in
+// thread order (deterministic for a fixed thread count).  Outputs are
+// overwritten.
+void or_rasterize_bwd(const float* means2d, const float* conics, const float* colors, int C,
+                      const float* opac, int64_t n, const int32_t* ids, const int32_t* ranges,
+                      const float* bg, int W, int H, const float* final_T, const int32_t* n_contrib,
+                      const float* grad_image, const float* grad_final_T, float* g_means2d,
+                      float* g_conics, float* g_colors, float* g_opac, int threads) {
+  const int tx = (W + TILE - 1) / TILE, ty = (H + TILE - 1) / TILE;
+  const int nt = n_threads(threads);
+  const int64_t stride = 6 + C;
+  std::vector<std::vector<float>> part(nt);
+#pragma omp parallel num_threads(nt)
+  {
+#ifdef _OPENMP
+    const int me = omp_get_thread_num();
+#else
+    const int me = 0;
+#endif
+    std::vector<float>& gp = part[me];
+    gp.assign(n * stride, 0.0f);
+    std::vector<float> dpix(C), accum(C), last_color(C);
+#pragma omp for schedule(static)
+    for (int tile = 0; tile < tx * ty; ++tile) {
+      const int start = ranges[2 * tile], end = ranges[2 * tile + 1];
+      for (int ly = 0; ly < TILE; ++ly)
+        for (int lx = 0; lx < TILE; ++lx) {
+          const int px = (tile % tx) * TILE + lx, py = (tile / tx) * TILE + ly;
+          if (px >= W || py >= H) continue;
+          const float pxf = (float)px + 0.5f, pyf = (float)py + 0.5f;
+          const int64_t pid = (int64_t)py * W + px;
+          const float T_final = final_T[pid];
+          float T = T_final;
+          const int last = n_contrib[pid];
+          float bg_dot = 0.0f;
+          for (int ch = 0; ch < C; ++ch) {
+            dpix[ch] = grad_image[pid * C + ch];
+            bg_dot += (bg ? bg[ch] : 0.0f) * dpix[ch];
+          }
+          if (grad_final_T) bg_dot += grad_final_T[pid];
+          std::fill(accum.begin(), accum.end(), 0.0f);
+          std::fill(last_color.begin(), last_color.end(), 0.0f);
+          float last_alpha = 0.0f;
+          for (int k = start + last - 1; k >= start; --k) {
+            const int g = ids[k];
+            const float dx = gs_sub(means2d[2 * g], pxf), dy = gs_sub(means2d[2 * g + 1], pyf);
+            const float* co = conics + 3 * g;
+            const float power = gs_sub(gs_mul(-0.5f, gs_add(gs_mul(gs_mul(co[0], dx), dx), gs_mul(gs_mul(co[2], dy), dy))),
+                                       gs_mul(gs_mul(co[1], dx), dy));
+            if (power > 0.0f) continue;
+            const float G = gs_expf(power);
+            const float alpha = gs_minf(0.99f, gs_mul(opac[g], G));
+            if (alpha < 1.0f / 255.0f) continue;
+            T = T / (1.0f - alpha);
+            const float aT = alpha * T;
+            float dL_dalpha = 0.0f;
+            for (int ch = 0; ch < C; ++ch) {
+              const float c = colors[(int64_t)g * C + ch];
+              accum[ch] = last_alpha * last_color[ch] + (1.0f - last_alpha) * accum[ch];
+              last_color[ch] = c;
+              dL_dalpha += (c - accum[ch]) * dpix[ch];
+            }
+            last_alpha = alpha;
+            dL_dalpha *= T;
+            dL_dalpha += (-T_final / (1.0f - alpha)) * bg_dot;
+            const float dL_dG = opac[g] * dL_dalpha;
+            const float gdx = G * dx, gdy = G * dy;
+            float* o = gp.data() + (int64_t)g * stride;
+            o[0] += -(gdx * co[0] + gdy * co[1]) * dL_dG;
+            o[1] += -(gdy * co[2] + gdx * co[1]) * dL_dG;
+            o[2] += -0.5f * gdx * dx * dL_dG;
+            o[3] += -gdx * dy * dL_dG;
+            o[4] += -0.5f * gdy * dy * dL_dG;
+            o[5] += G * dL_dalpha;
+            for (int ch = 0; ch < C; ++ch) o[6 + ch] += aT * dpix[ch];
+          }
+        }
+    }
+  }
+  for (int64_t g = 0; g < n; ++g) {
+    float s[6] = {0, 0, 0, 0, 0, 0};
+    for (int t = 0; t < nt; ++t)
+      for (int k = 0; k < 6; ++k) s[k] += part[t][g * stride + k];
+    g_means2d[2 * g] = s[0];
+    g_means2d[2 * g + 1] = s[1];
+    g_conics[3 * g] = s[2];
+    g_conics[3 * g + 1] = s[3];
+    g_conics[3 * g + 2] = s[4];
+    g_opac[g] = s[5];
+    for (int ch = 0; ch < C; ++ch) {
+      float v = 0.0f;
+      for (int t = 0; t < nt; ++t) v += part[t][g * stride + 6 + ch];
+      g_colors[g * C + ch] = v;
+    }
+  }
+}
+
+// The shared exponential, exported so tests can check it against libm.
+float or_expf(float x) { return gs_expf(x); }
+
+}  // extern "C"

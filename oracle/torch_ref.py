@@ -1,0 +1,156 @@
+"""CPU ORACLE — TEST INFRASTRUCTURE ONLY (autograd restatements).
+
+Differentiable torch restatements of the reference's pure-MLX pieces, used to
+check the hand-derived sm_100a backward kernels against automatic
+differentiation (the reference gets these gradients from MLX autodiff):
+
+* ``project``     — src/mlx3d/splatting/projection.py:24-146
+* ``eval_sh``     — src/mlx3d/splatting/sh.py:41-78
+* ``view_dirs``   — src/mlx3d/splatting/render.py:77-78
+* ``naive_render``— src/mlx3d/splatting/reference.py:16-74, the reference's own
+  O(N*H*W) test oracle (small scenes only).
+
+The product package never imports this module.
+"""
+
+from __future__ import annotations
+
+import torch
+
+SH_C0 = 0.28209479177387814
+SH_C1 = 0.4886025119029199
+SH_C2 = (1.0925484305920792, -1.0925484305920792, 0.31539156525252005, -1.0925484305920792, 0.5462742152960396)
+SH_C3 = (-0.5900435899266435, 2.890611442640554, -0.4570457994644658, 0.3731763325901154, -0.4570457994644658,
+         1.445305721320277, -0.5900435899266435)
+
+
+def project(camera, means, quats, scales, blur=0.3, antialias=False):
+    dt = means.dtype
+    R = camera.R.to(dt)
+    t = camera.t.to(dt)
+    mx_, my_, mz_ = means[:, 0], means[:, 1], means[:, 2]
+    x = mx_ * R[0, 0] + my_ * R[0, 1] + mz_ * R[0, 2] + t[0]
+    y = mx_ * R[1, 0] + my_ * R[1, 1] + mz_ * R[1, 2] + t[1]
+    z = mx_ * R[2, 0] + my_ * R[2, 1] + mz_ * R[2, 2] + t[2]
+    z_safe = torch.clamp(z, min=1e-6)
+    u = camera.fx * x / z_safe + camera.cx
+    v = camera.fy * y / z_safe + camera.cy
+    tan_fov_x = 0.5 * camera.width / camera.fx
+    tan_fov_y = 0.5 * camera.height / camera.fy
+    tx = torch.clamp(x / z_safe, -1.3 * tan_fov_x, 1.3 * tan_fov_x) * z_safe
+    ty = torch.clamp(y / z_safe, -1.3 * tan_fov_y, 1.3 * tan_fov_y) * z_safe
+    inv_z = 1.0 / z_safe
+    inv_z2 = inv_z * inv_z
+    j00 = camera.fx * inv_z
+    j02 = -camera.fx * tx * inv_z2
+    j11 = camera.fy * inv_z
+    j12 = -camera.fy * ty * inv_z2
+    t00 = j00 * R[0, 0] + j02 * R[2, 0]
+    t01 = j00 * R[0, 1] + j02 * R[2, 1]
+    t02 = j00 * R[0, 2] + j02 * R[2, 2]
+    t10 = j11 * R[1, 0] + j12 * R[2, 0]
+    t11 = j11 * R[1, 1] + j12 * R[2, 1]
+    t12 = j11 * R[1, 2] + j12 * R[2, 2]
+    q = quats / torch.linalg.norm(quats, dim=-1, keepdim=True)
+    qw, qx, qy, qz = q[:, 0], q[:, 1], q[:, 2], q[:, 3]
+    r00 = 1.0 - 2.0 * (qy * qy + qz * qz)
+    r01 = 2.0 * (qx * qy - qw * qz)
+    r02 = 2.0 * (qx * qz + qw * qy)
+    r10 = 2.0 * (qx * qy + qw * qz)
+    r11 = 1.0 - 2.0 * (qx * qx + qz * qz)
+    r12 = 2.0 * (qy * qz - qw * qx)
+    r20 = 2.0 * (qx * qz - qw * qy)
+    r21 = 2.0 * (qy * qz + qw * qx)
+    r22 = 1.0 - 2.0 * (qx * qx + qy * qy)
+    sx, sy, sz = scales[:, 0], scales[:, 1], scales[:, 2]
+    m00 = (t00 * r00 + t01 * r10 + t02 * r20) * sx
+    m01 = (t00 * r01 + t01 * r11 + t02 * r21) * sy
+    m02 = (t00 * r02 + t01 * r12 + t02 * r22) * sz
+    m10 = (t10 * r00 + t11 * r10 + t12 * r20) * sx
+    m11 = (t10 * r01 + t11 * r11 + t12 * r21) * sy
+    m12 = (t10 * r02 + t11 * r12 + t12 * r22) * sz
+    a0 = m00 * m00 + m01 * m01 + m02 * m02
+    b = m00 * m10 + m01 * m11 + m02 * m12
+    c0 = m10 * m10 + m11 * m11 + m12 * m12
+    a = a0 + blur
+    c = c0 + blur
+    det = a * c - b * b
+    det_safe = torch.clamp(det, min=1e-12)
+    conics = torch.stack([c / det_safe, -b / det_safe, a / det_safe], dim=-1)
+    if antialias and blur > 0:
+        det0 = torch.clamp(a0 * c0 - b * b, min=0.0)
+        comp = torch.sqrt(det0 / det_safe)
+    else:
+        comp = torch.ones_like(det)
+    mid = 0.5 * (a + c)
+    lam1 = mid + torch.sqrt(torch.clamp(mid * mid - det, min=0.01))
+    radii = torch.ceil(3.0 * torch.sqrt(torch.clamp(lam1, min=0.0)))
+    valid = (z > camera.znear) & (det > 0)
+    radii = torch.where(valid, radii, torch.zeros_like(radii)).detach()
+    comp = torch.where(valid, comp, torch.zeros_like(comp))
+    return {"means2d": torch.stack([u, v], dim=-1), "conics": conics, "depths": z, "radii": radii,
+            "compensation": comp}
+
+
+def eval_sh(degree, sh, dirs):
+    result = SH_C0 * sh[:, 0]
+    if degree > 0:
+        x, y, z = dirs[:, 0:1], dirs[:, 1:2], dirs[:, 2:3]
+        result = result - SH_C1 * y * sh[:, 1] + SH_C1 * z * sh[:, 2] - SH_C1 * x * sh[:, 3]
+        if degree > 1:
+            xx, yy, zz = x * x, y * y, z * z
+            xy, yz, xz = x * y, y * z, x * z
+            result = (result + SH_C2[0] * xy * sh[:, 4] + SH_C2[1] * yz * sh[:, 5]
+                      + SH_C2[2] * (2.0 * zz - xx - yy) * sh[:, 6] + SH_C2[3] * xz * sh[:, 7]
+                      + SH_C2[4] * (xx - yy) * sh[:, 8])
+            if degree > 2:
+                result = (result + SH_C3[0] * y * (3.0 * xx - yy) * sh[:, 9] + SH_C3[1] * xy * z * sh[:, 10]
+                          + SH_C3[2] * y * (4.0 * zz - xx - yy) * sh[:, 11]
+                          + SH_C3[3] * z * (2.0 * zz - 3.0 * xx - 3.0 * yy) * sh[:, 12]
+                          + SH_C3[4] * x * (4.0 * zz - xx - yy) * sh[:, 13] + SH_C3[5] * z * (xx - yy) * sh[:, 14]
+                          + SH_C3[6] * x * (xx - 3.0 * yy) * sh[:, 15])
+    return result + 0.5
+
+
+def view_dirs(camera, means):
+    center = (-(camera.R.T.to(torch.float32) @ camera.t.to(torch.float32))).to(means.dtype)
+    d = means - center
+    return d / torch.clamp(torch.linalg.norm(d, dim=-1, keepdim=True), min=1e-8)
+
+
+def naive_render(camera, means, quats, scales, opacities, colors, background=None, antialias=False):
+    """reference.py:16-74: every Gaussian at every pixel, global depth order."""
+    dt = means.dtype
+    if background is None:
+        background = torch.zeros(3, dtype=dt)
+    H, W = camera.height, camera.width
+    proj = project(camera, means, quats, scales, antialias=antialias)
+    order = torch.argsort(proj["depths"].detach(), stable=True)
+    means2d = proj["means2d"][order]
+    conics = proj["conics"][order]
+    colors = colors[order]
+    opac = (opacities * proj["compensation"])[order]
+    radii = proj["radii"][order]
+    xs = torch.arange(W, dtype=dt) + 0.5
+    ys = torch.arange(H, dtype=dt) + 0.5
+    px = xs[None, :].expand(H, W)
+    py = ys[:, None].expand(H, W)
+    dx = means2d[:, 0][:, None, None] - px[None]
+    dy = means2d[:, 1][:, None, None] - py[None]
+    a = conics[:, 0][:, None, None]
+    b = conics[:, 1][:, None, None]
+    c = conics[:, 2][:, None, None]
+    power = -0.5 * (a * dx * dx + c * dy * dy) - b * dx * dy
+    alpha = torch.clamp(opac[:, None, None] * torch.exp(power), max=0.99)
+    alpha = torch.where(power > 0.0, torch.zeros_like(alpha), alpha)
+    alpha = torch.where(alpha < 1.0 / 255.0, torch.zeros_like(alpha), alpha)
+    alpha = alpha * (radii > 0)[:, None, None]
+    one_minus = 1.0 - alpha
+    trans = torch.cumprod(one_minus, dim=0)
+    trans = torch.cat([torch.ones_like(trans[:1]), trans[:-1]], dim=0)
+    keep = trans > 1e-4
+    weights = alpha * trans * keep
+    image = torch.sum(weights[..., None] * colors[:, None, None, :], dim=0)
+    final_T = torch.prod(torch.where(keep, one_minus, torch.ones_like(one_minus)), dim=0)
+    image = image + final_T[..., None] * background
+    return {"image": image, "alpha": 1.0 - final_T, "final_T": final_T}
