@@ -273,8 +273,8 @@ k_scan_down(const int32_t* __restrict__ counts, const int32_t* __restrict__ perm
 // every tile of its rectangle, row-major (tiles.py:77-89).
 __global__ void k_duplicate(const float* __restrict__ means2d, const float* __restrict__ radii,
                             const int32_t* __restrict__ perm, const uint32_t* __restrict__ offsets,
-                            int64_t n, int width, int height, int tiles_x, int tiles_y,
-                            uint32_t* __restrict__ tkeys, int32_t* __restrict__ tvals) {
+                            int64_t n, int64_t d, int width, int height, int tiles_x,
+                            int tiles_y, uint32_t* __restrict__ tkeys, int32_t* __restrict__ tvals) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int32_t g = perm[i];
@@ -292,6 +292,7 @@ __global__ void k_duplicate(const float* __restrict__ means2d, const float* __re
   uint32_t o = offsets[i];
   for (int ty = y0; ty <= y1; ++ty)
     for (int tx = x0; tx <= x1; ++tx) {
+      if ((int64_t)o >= d) return;  // never past the caller's D (counts are recomputed exactly)
       tkeys[o] = (uint32_t)(ty * tiles_x + tx);
       tvals[o] = g;
       ++o;
@@ -461,7 +462,7 @@ int gs_bin_end(const float* means2d, const float* radii, int64_t n, int64_t d, i
   uint32_t* tk1 = at<uint32_t>(ws_d, M.keys1);
   int32_t* tv0 = at<int32_t>(ws_d, M.vals0);
   int32_t* tv1 = at<int32_t>(ws_d, M.vals1);
-  k_duplicate<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(means2d, radii, perm, offsets, n, width,
+  k_duplicate<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(means2d, radii, perm, offsets, n, d, width,
                                                          height, tiles_x, tiles_y, tk0, tv0);
   if (int e = check_launch("k_duplicate")) return e;
   const int bits = tile_bits(num_tiles);

@@ -18,7 +18,7 @@
 // with correctly rounded fused multiply-adds).  It is bit-identical on host and
 // device because it uses only IEEE-exact primitives (fmaf, rintf, exact
 // power-of-two scaling).  Its error against the true exponential is below
-// 2 ulp on the whole float range; tests/test_math.py checks this.
+// 2 ulp on the whole float range; tests/test_oracle.py checks this.
 #pragma once
 
 #include <stdint.h>
@@ -103,9 +103,6 @@ GS_HD float gs_pow2i(int k) { return gs_bits_to_float((uint32_t)(k + 127) << 23)
 // (truncation error < 5e-9 relative for |r| <= 0.347); result scaled by 2^n
 // in at most two exact power-of-two steps so sub-normal results round once.
 GS_HD float gs_expf(float x) {
-  if (x != x) return x;                       // NaN
-  if (x > 88.72283935546875f) return INFINITY;  // above ln(FLT_MAX)
-  if (x < -103.972084045410156f) return 0.0f;  // below ln(smallest denormal / 2)
   const float kLog2e = 1.44269502162933349609375f;   // nearest float to 1/ln2
   const float kLn2Hi = 0.693147182464599609375f;     // nearest float to ln2
   const float kLn2Lo = -1.904654299957768e-09f;      // ln2 - kLn2Hi
@@ -121,6 +118,11 @@ GS_HD float gs_expf(float x) {
   p = gs_fma(p, r, 0.5f);
   p = gs_fma(p, r, 1.0f);
   p = gs_fma(p, r, 1.0f);
+  // Fast path: n in [-126, 127], one exact power-of-two scaling.
+  if (x >= -87.0f && x <= 88.0f) return gs_mul(p, gs_pow2i((int)n));
+  if (x != x) return x;                       // NaN
+  if (x > 88.72283935546875f) return INFINITY;  // above ln(FLT_MAX)
+  if (x < -103.972084045410156f) return 0.0f;  // below ln(smallest denormal / 2)
   int k = (int)n;
   if (k > 127) return gs_mul(gs_mul(p, gs_pow2i(127)), gs_pow2i(k - 127));
   if (k >= -126) return gs_mul(p, gs_pow2i(k));

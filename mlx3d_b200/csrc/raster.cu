@@ -31,91 +31,170 @@ __device__ __forceinline__ float power_floor(float o) {
   return o > 0.0f ? -logf(255.0f * o) - 1e-3f : INFINITY;
 }
 
+// Conservative pixel-space box (xmin, xmax, ymin, ymax) around every pixel
+// centre where power >= pf can hold, i.e. the ellipse
+// A dx^2 + 2 B dx dy + C dy^2 <= 2 L with L = -pf: half extents
+// sqrt(2 L C / det) and sqrt(2 L A / det).  The box is widened by 2 % + 1 px,
+// far beyond the float32 evaluation error of power near the ellipse, so a
+// warp whose pixels all lie outside it can skip the Gaussian: every one of
+// its pixels would fail the exact power >= pf test anyway.  A Gaussian that
+// can never reach alpha >= 1/255 gets an empty box; a degenerate conic an
+// unbounded one.
+__device__ __forceinline__ float4 cull_box(float2 m, float4 co, float pf) {
+  const float L = -pf;
+  if (!(L > 0.0f)) return make_float4(INFINITY, -INFINITY, INFINITY, -INFINITY);
+  const float det = co.x * co.z - co.y * co.y;
+  if (!(det > 0.0f) || !(co.x > 0.0f) || !(co.z > 0.0f))
+    return make_float4(-INFINITY, INFINITY, -INFINITY, INFINITY);
+  const float hx = sqrtf(2.0f * L * co.z / det) * 1.02f + 1.0f;
+  const float hy = sqrtf(2.0f * L * co.x / det) * 1.02f + 1.0f;
+  return make_float4(m.x - hx, m.x + hx, m.y - hy, m.y + hy);
+}
+
+// Pixel layout shared by both compositors: 128 threads per 16x16 tile, warp
+// w owns the 8x8 quadrant (w & 1, w >> 1), lane l the two vertically
+// adjacent pixels (l & 7, 2 (l >> 3) + {0, 1}) of it.
+struct TilePixels {
+  int px, py0;
+  float wx0, wx1, wy0, wy1;  // pixel-centre extent of the warp's quadrant
+  __device__ TilePixels(int tile, int tiles_x) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int qx = (tile % tiles_x) * GS_TILE + (warp & 1) * 8;
+    const int qy = (tile / tiles_x) * GS_TILE + (warp >> 1) * 8;
+    px = qx + (lane & 7);
+    py0 = qy + 2 * (lane >> 3);
+    wx0 = (float)qx + 0.5f;
+    wx1 = (float)qx + 7.5f;
+    wy0 = (float)qy + 0.5f;
+    wy1 = (float)qy + 7.5f;
+  }
+  __device__ bool misses(float4 bb) const {
+    return bb.y < wx0 || bb.x > wx1 || bb.w < wy0 || bb.z > wy1;
+  }
+};
+
+// Forward compositor.  One CTA of 128 threads per tile (TilePixels layout);
+// each thread owns two pixels, so every staged Gaussian is read from shared
+// memory once per two pixels, and a warp skips Gaussians whose cull_box
+// misses its quadrant.  Front-to-back blending per pixel exactly as
+// rasterize.py:74-87: skip power > 0, skip alpha < 1/255, stop before
+// compositing once T would drop below 1e-4.  The CTA leaves the tile when
+// all of its pixels have stopped (counted at every batch boundary).
+constexpr int kFwdThreads = 128;
+constexpr int kFwdBatch = 256;
+
 template <int CMAX, bool DEPTH>
-__global__ void __launch_bounds__(GS_BLOCK) k_raster_fwd(const RasterArgs a) {
-  __shared__ float2 s_xy[GS_BLOCK];
-  __shared__ float4 s_co[GS_BLOCK];  // conic a, b, c, opacity
-  __shared__ float s_pf[GS_BLOCK];   // power floor
-  __shared__ float s_col[CMAX > 0 ? CMAX : 1][GS_BLOCK];
-  __shared__ float s_z[DEPTH ? GS_BLOCK : 1];
+__global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) {
+  constexpr int NC = CMAX > 0 ? CMAX : 1;
+  __shared__ float2 s_xy[kFwdBatch];
+  __shared__ float4 s_co[kFwdBatch];  // conic a, b, c, opacity
+  __shared__ float s_pf[kFwdBatch];   // power floor
+  __shared__ float4 s_bb[kFwdBatch];  // cull box
+  __shared__ float s_col[NC][kFwdBatch];
+  __shared__ float s_z[DEPTH ? kFwdBatch : 1];
 
   const int tile = blockIdx.x;
-  const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
-  const int px = tx * GS_TILE + (threadIdx.x & 15);
-  const int py = ty * GS_TILE + (threadIdx.x >> 4);
-  const bool inside = px < a.width && py < a.height;
-  const float pxf = (float)px + 0.5f, pyf = (float)py + 0.5f;
+  const TilePixels tp(tile, a.tiles_x);
+  const int px = tp.px, py0 = tp.py0;
+  const float pxf = (float)px + 0.5f;
   const int start = a.ranges[2 * tile], end = a.ranges[2 * tile + 1];
   const int num = end - start;
 
-  float T = 1.0f;
-  float acc[CMAX > 0 ? CMAX : 1];
+  bool inside[2], done[2];
+  float pyf[2], T[2], dacc[2];
+  float acc[2][NC];
+  int last[2];
 #pragma unroll
-  for (int ch = 0; ch < (CMAX > 0 ? CMAX : 1); ++ch) acc[ch] = 0.0f;
-  float dacc = 0.0f;
-  int last = 0;
-  bool done = !inside;
+  for (int p = 0; p < 2; ++p) {
+    inside[p] = px < a.width && py0 + p < a.height;
+    done[p] = !inside[p];
+    pyf[p] = (float)(py0 + p) + 0.5f;
+    T[p] = 1.0f;
+    dacc[p] = 0.0f;
+    last[p] = 0;
+#pragma unroll
+    for (int ch = 0; ch < NC; ++ch) acc[p][ch] = 0.0f;
+  }
 
-  for (int b0 = 0; b0 < num; b0 += GS_BLOCK) {
+  for (int b0 = 0; b0 < num; b0 += kFwdBatch) {
     // Barrier before the batch overwrites shared memory; also ends the tile
     // once every pixel has terminated.
-    if (__syncthreads_count(done) == GS_BLOCK) break;
-    const int li = start + b0 + threadIdx.x;
-    if (li < end) {
-      const int g = __ldg(a.ids + li);
-      s_xy[threadIdx.x] = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
-      const float o = __ldg(a.opac + g);
-      s_co[threadIdx.x] = make_float4(__ldg(a.conics + 3 * g), __ldg(a.conics + 3 * g + 1),
-                                      __ldg(a.conics + 3 * g + 2), o);
-      s_pf[threadIdx.x] = power_floor(o);
+    if (__syncthreads_count(done[0] && done[1]) == kFwdThreads) break;
 #pragma unroll
-      for (int ch = 0; ch < CMAX; ++ch)
-        if (ch < a.cc) s_col[ch][threadIdx.x] = __ldg(a.colors + (int64_t)g * a.c_total + a.c0 + ch);
-      if (DEPTH) s_z[threadIdx.x] = __ldg(a.depths + g);
+    for (int r = 0; r < kFwdBatch / kFwdThreads; ++r) {
+      const int t = threadIdx.x + r * kFwdThreads;
+      const int li = start + b0 + t;
+      if (li < end) {
+        const int g = __ldg(a.ids + li);
+        const float2 m = __ldg(reinterpret_cast<const float2*>(a.means2d) + g);
+        const float o = __ldg(a.opac + g);
+        const float4 co = make_float4(__ldg(a.conics + 3 * g), __ldg(a.conics + 3 * g + 1),
+                                      __ldg(a.conics + 3 * g + 2), o);
+        const float pf = power_floor(o);
+        s_xy[t] = m;
+        s_co[t] = co;
+        s_pf[t] = pf;
+        s_bb[t] = cull_box(m, co, pf);
+#pragma unroll
+        for (int ch = 0; ch < CMAX; ++ch)
+          if (ch < a.cc) s_col[ch][t] = __ldg(a.colors + (int64_t)g * a.c_total + a.c0 + ch);
+        if (DEPTH) s_z[t] = __ldg(a.depths + g);
+      }
     }
     __syncthreads();
-    if (done) continue;
-    const int bs = min(GS_BLOCK, num - b0);
+    const int bs = min(kFwdBatch, num - b0);
     for (int j = 0; j < bs; ++j) {
+      if (done[0] && done[1]) break;
+      if (tp.misses(s_bb[j])) continue;
       const float2 m = s_xy[j];
       const float4 co = s_co[j];
-      const float dx = gs_sub(m.x, pxf), dy = gs_sub(m.y, pyf);
-      const float power = gs_sub(
-          gs_mul(-0.5f, gs_add(gs_mul(gs_mul(co.x, dx), dx), gs_mul(gs_mul(co.z, dy), dy))),
-          gs_mul(gs_mul(co.y, dx), dy));
-      if (power > 0.0f || power < s_pf[j]) continue;
-      const float alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, gs_expf(power)));
-      if (alpha < GS_ALPHA_MIN) continue;
-      const float next_T = gs_mul(T, gs_sub(1.0f, alpha));
-      if (next_T < GS_T_MIN) {
-        done = true;
-        break;
-      }
-      const float w = gs_mul(alpha, T);
+      const float pf = s_pf[j];
+      const float dx = gs_sub(m.x, pxf);
+      const float adxdx = gs_mul(gs_mul(co.x, dx), dx);
+      const float bdx = gs_mul(co.y, dx);
 #pragma unroll
-      for (int ch = 0; ch < CMAX; ++ch) acc[ch] = gs_add(acc[ch], gs_mul(s_col[ch][j], w));
-      if (DEPTH) dacc = gs_add(dacc, gs_mul(s_z[j], w));
-      T = next_T;
-      last = b0 + j + 1;
-    }
-  }
-  if (!inside) return;
-  const int64_t pid = (int64_t)py * a.width + px;
-  if (a.image) {
+      for (int p = 0; p < 2; ++p) {
+        if (done[p]) continue;
+        const float dy = gs_sub(m.y, pyf[p]);
+        const float power =
+            gs_sub(gs_mul(-0.5f, gs_add(adxdx, gs_mul(gs_mul(co.z, dy), dy))), gs_mul(bdx, dy));
+        if (power > 0.0f || power < pf) continue;
+        const float alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, gs_expf(power)));
+        if (alpha < GS_ALPHA_MIN) continue;
+        const float next_T = gs_mul(T[p], gs_sub(1.0f, alpha));
+        if (next_T < GS_T_MIN) {
+          done[p] = true;
+          continue;
+        }
+        const float w = gs_mul(alpha, T[p]);
 #pragma unroll
-    for (int ch = 0; ch < CMAX; ++ch) {
-      if (ch < a.cc) {
-        const float bgv = a.bg ? a.bg[a.c0 + ch] : 0.0f;
-        a.image[pid * a.c_total + a.c0 + ch] = gs_add(acc[ch], gs_mul(T, bgv));
+        for (int ch = 0; ch < CMAX; ++ch) acc[p][ch] = gs_add(acc[p][ch], gs_mul(s_col[ch][j], w));
+        if (DEPTH) dacc[p] = gs_add(dacc[p], gs_mul(s_z[j], w));
+        T[p] = next_T;
+        last[p] = b0 + j + 1;
       }
     }
   }
-  if (a.write_aux) {
-    if (a.final_T) a.final_T[pid] = T;
-    if (a.n_contrib) a.n_contrib[pid] = last;
-    if (DEPTH && a.depth) {
-      const float al = gs_sub(1.0f, T);
-      a.depth[pid] = al > 1e-6f ? gs_div(dacc, al) : 0.0f;
+#pragma unroll
+  for (int p = 0; p < 2; ++p) {
+    if (!inside[p]) continue;
+    const int64_t pid = (int64_t)(py0 + p) * a.width + px;
+    if (a.image) {
+#pragma unroll
+      for (int ch = 0; ch < CMAX; ++ch) {
+        if (ch < a.cc) {
+          const float bgv = a.bg ? a.bg[a.c0 + ch] : 0.0f;
+          a.image[pid * a.c_total + a.c0 + ch] = gs_add(acc[p][ch], gs_mul(T[p], bgv));
+        }
+      }
+    }
+    if (a.write_aux) {
+      if (a.final_T) a.final_T[pid] = T[p];
+      if (a.n_contrib) a.n_contrib[pid] = last[p];
+      if (DEPTH && a.depth) {
+        const float al = gs_sub(1.0f, T[p]);
+        a.depth[pid] = al > 1e-6f ? gs_div(dacc[p], al) : 0.0f;
+      }
     }
   }
 }
@@ -127,153 +206,226 @@ struct RasterBwdArgs {
   float *g_means2d, *g_conics, *g_colors, *g_opac;
 };
 
-// Gradient slots per staged Gaussian: 0-1 means2d, 2-4 conic, 5 opacity,
+// Sum over the 32 lanes of a warp of eight per-lane values v[0..7], leaving
+// the total of value ((lane>>4)&1)*4 + ((lane>>3)&1)*2 + ((lane>>2)&1) in
+// every lane: three halving exchanges (4 + 2 + 1 shuffles) followed by a
+// two-step butterfly — 9 shuffles instead of 8 x 5 for separate butterflies.
+__device__ __forceinline__ float warp_reduce8(const float* v, int lane) {
+  const bool u16 = lane & 16, u8 = lane & 8, u4 = lane & 4;
+  float a[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float send = u16 ? v[i] : v[i + 4];
+    const float keep = u16 ? v[i + 4] : v[i];
+    a[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+  float b[2];
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float send = u8 ? a[i] : a[i + 2];
+    const float keep = u8 ? a[i + 2] : a[i];
+    b[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+  const float send = u4 ? b[0] : b[1];
+  float c = (u4 ? b[1] : b[0]) + __shfl_xor_sync(0xffffffffu, send, 4);
+  c += __shfl_xor_sync(0xffffffffu, c, 2);
+  c += __shfl_xor_sync(0xffffffffu, c, 1);
+  return c;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+// Backward compositor.  One CTA of 128 threads per tile (TilePixels layout),
+// each thread owning two pixels of its warp's 8x8 quadrant.  For every
+// staged Gaussian j (back to front) each thread sums its two pixels'
+// gradient contributions in registers, the warp reduces them
+// (warp_reduce8), the per-warp totals go to shared memory without atomics,
+// and after the batch one thread per Gaussian adds the warps' totals to the
+// global gradients with one atomic per value.
+//
+// Gradient values per Gaussian: 0-1 means2d, 2-4 conic, 5 opacity,
 // 6.. colour channels.
+constexpr int kBwdThreads = 128;
+constexpr int kBwdWarps = kBwdThreads / 32;
+
 template <int CMAX>
-__global__ void __launch_bounds__(GS_BLOCK) k_raster_bwd(const RasterBwdArgs g) {
+__global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs g) {
   const RasterArgs& a = g.f;
-  constexpr int NG = 6 + CMAX;
-  __shared__ int s_id[GS_BLOCK];
-  __shared__ float2 s_xy[GS_BLOCK];
-  __shared__ float4 s_co[GS_BLOCK];
-  __shared__ float s_col[CMAX][GS_BLOCK];
-  __shared__ float s_g[NG][GS_BLOCK];
-  __shared__ int s_hit[GS_BLOCK];
+  constexpr int NV = 6 + CMAX;
+  constexpr int NV8 = (NV / 8) * 8;  // values reduced by warp_reduce8
+  constexpr int BATCH = CMAX <= 4 ? 128 : 64;
+  __shared__ int s_id[BATCH];
+  __shared__ float2 s_xy[BATCH];
+  __shared__ float4 s_co[BATCH];
+  __shared__ float s_pf[BATCH];
+  __shared__ float4 s_bb[BATCH];
+  __shared__ float s_col[CMAX][BATCH];
+  // per-warp gradient totals; the +1 pitch puts the eight values a warp
+  // stores for one Gaussian in eight different banks
+  __shared__ float s_gw[kBwdWarps][NV][BATCH + 1];
   __shared__ int s_max_last;
 
   const int tile = blockIdx.x;
-  const int tx = tile % a.tiles_x, ty = tile / a.tiles_x;
-  const int px = tx * GS_TILE + (threadIdx.x & 15);
-  const int py = ty * GS_TILE + (threadIdx.x >> 4);
-  const bool inside = px < a.width && py < a.height;
-  const float pxf = (float)px + 0.5f, pyf = (float)py + 0.5f;
-  const int64_t pid = (int64_t)py * a.width + px;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const TilePixels tp(tile, a.tiles_x);
+  const int px = tp.px, py0 = tp.py0;
+  const float pxf = (float)px + 0.5f;
   const int start = a.ranges[2 * tile], end = a.ranges[2 * tile + 1];
   const int num = end - start;
-  const int lane = threadIdx.x & 31;
 
-  const float T_final = inside ? a.final_T[pid] : 1.0f;
-  float T = T_final;
-  const int last = inside ? a.n_contrib[pid] : 0;
-  float dpix[CMAX];
-  float bg_dot = 0.0f;
+  bool inside[2];
+  float pyf[2], T[2], T_final[2], bg_dot[2], last_alpha[2];
+  int last[2];
+  float dpix[2][CMAX], accum[2][CMAX], last_color[2][CMAX];
 #pragma unroll
-  for (int ch = 0; ch < CMAX; ++ch) {
-    dpix[ch] = 0.0f;
-    if (inside && ch < a.cc) {
-      dpix[ch] = g.grad_image[pid * a.c_total + a.c0 + ch];
-      if (a.bg) bg_dot += a.bg[a.c0 + ch] * dpix[ch];
+  for (int p = 0; p < 2; ++p) {
+    const int py = py0 + p;
+    inside[p] = px < a.width && py < a.height;
+    pyf[p] = (float)py + 0.5f;
+    const int64_t pid = (int64_t)py * a.width + px;
+    T_final[p] = inside[p] ? a.final_T[pid] : 1.0f;
+    T[p] = T_final[p];
+    last[p] = inside[p] ? a.n_contrib[pid] : 0;
+    bg_dot[p] = 0.0f;
+    last_alpha[p] = 0.0f;
+#pragma unroll
+    for (int ch = 0; ch < CMAX; ++ch) {
+      dpix[p][ch] = 0.0f;
+      accum[p][ch] = 0.0f;
+      last_color[p][ch] = 0.0f;
+      if (inside[p] && ch < a.cc) {
+        dpix[p][ch] = g.grad_image[pid * a.c_total + a.c0 + ch];
+        if (a.bg) bg_dot[p] += a.bg[a.c0 + ch] * dpix[p][ch];
+      }
     }
+    if (inside[p] && g.use_grad_final_T && g.grad_final_T) bg_dot[p] += g.grad_final_T[pid];
   }
-  if (inside && g.use_grad_final_T && g.grad_final_T) bg_dot += g.grad_final_T[pid];
-  float accum[CMAX], last_color[CMAX];
-#pragma unroll
-  for (int ch = 0; ch < CMAX; ++ch) accum[ch] = last_color[ch] = 0.0f;
-  float last_alpha = 0.0f;
 
-  // Nothing at or beyond the largest n_contrib of this warp (block) matters.
-  int wmax = last;
+  // Nothing at or beyond the largest n_contrib of a warp (block) matters.
+  int wmax = max(last[0], last[1]);
+#pragma unroll
   for (int o = 16; o > 0; o >>= 1) wmax = max(wmax, __shfl_xor_sync(0xffffffffu, wmax, o));
   if (threadIdx.x == 0) s_max_last = 0;
   __syncthreads();
   if (lane == 0) atomicMax(&s_max_last, wmax);
   __syncthreads();
-  const int block_last = s_max_last;
-  const int nbat = (block_last + GS_BLOCK - 1) / GS_BLOCK;
+  const int nbat = (s_max_last + BATCH - 1) / BATCH;
 
   for (int b = nbat - 1; b >= 0; --b) {
-    const int b0 = b * GS_BLOCK;
+    const int b0 = b * BATCH;
     __syncthreads();
-    const int li = start + b0 + threadIdx.x;
-    if (li < end) {
-      const int gid = __ldg(a.ids + li);
-      s_id[threadIdx.x] = gid;
-      s_xy[threadIdx.x] = __ldg(reinterpret_cast<const float2*>(a.means2d) + gid);
-      s_co[threadIdx.x] = make_float4(__ldg(a.conics + 3 * gid), __ldg(a.conics + 3 * gid + 1),
-                                      __ldg(a.conics + 3 * gid + 2), __ldg(a.opac + gid));
+    if (threadIdx.x < BATCH) {
+      const int li = start + b0 + threadIdx.x;
+      if (li < end) {
+        const int gid = __ldg(a.ids + li);
+        s_id[threadIdx.x] = gid;
+        const float2 m = __ldg(reinterpret_cast<const float2*>(a.means2d) + gid);
+        const float o = __ldg(a.opac + gid);
+        const float4 co = make_float4(__ldg(a.conics + 3 * gid), __ldg(a.conics + 3 * gid + 1),
+                                      __ldg(a.conics + 3 * gid + 2), o);
+        const float pf = power_floor(o);
+        s_xy[threadIdx.x] = m;
+        s_co[threadIdx.x] = co;
+        s_pf[threadIdx.x] = pf;
+        s_bb[threadIdx.x] = cull_box(m, co, pf);
 #pragma unroll
-      for (int ch = 0; ch < CMAX; ++ch)
-        s_col[ch][threadIdx.x] =
-            ch < a.cc ? __ldg(a.colors + (int64_t)gid * a.c_total + a.c0 + ch) : 0.0f;
+        for (int ch = 0; ch < CMAX; ++ch)
+          s_col[ch][threadIdx.x] =
+              ch < a.cc ? __ldg(a.colors + (int64_t)gid * a.c_total + a.c0 + ch) : 0.0f;
+      }
     }
-#pragma unroll
-    for (int k = 0; k < NG; ++k) s_g[k][threadIdx.x] = 0.0f;
-    s_hit[threadIdx.x] = 0;
+    for (int e = threadIdx.x; e < kBwdWarps * NV * (BATCH + 1); e += kBwdThreads) (&s_gw[0][0][0])[e] = 0.0f;
     __syncthreads();
-    const int bs = min(GS_BLOCK, num - b0);
+    const int bs = min(BATCH, num - b0);
     const int jtop = min(bs, wmax - b0) - 1;
     for (int j = jtop; j >= 0; --j) {
-      bool contrib = inside && (b0 + j < last);
-      float G = 0.0f, alpha = 0.0f, dx = 0.0f, dy = 0.0f;
+      if (tp.misses(s_bb[j])) continue;
       const float4 co = s_co[j];
-      if (contrib) {
-        const float2 m = s_xy[j];
-        dx = gs_sub(m.x, pxf);
-        dy = gs_sub(m.y, pyf);
+      const float2 m = s_xy[j];
+      const float pf = s_pf[j];
+      float gv[NV];
+#pragma unroll
+      for (int k = 0; k < NV; ++k) gv[k] = 0.0f;
+      bool any = false;
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        if (!(inside[p] && b0 + j < last[p])) continue;
+        const float dx = gs_sub(m.x, pxf), dy = gs_sub(m.y, pyf[p]);
         const float power = gs_sub(
             gs_mul(-0.5f, gs_add(gs_mul(gs_mul(co.x, dx), dx), gs_mul(gs_mul(co.z, dy), dy))),
             gs_mul(gs_mul(co.y, dx), dy));
-        if (power > 0.0f) {
-          contrib = false;
-        } else {
-          G = gs_expf(power);
-          alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, G));
-          if (alpha < GS_ALPHA_MIN) contrib = false;
-        }
-      }
-      float gv[NG];
-#pragma unroll
-      for (int k = 0; k < NG; ++k) gv[k] = 0.0f;
-      if (contrib) {
-        T = T / (1.0f - alpha);
-        const float aT = alpha * T;
+        if (power > 0.0f || power < pf) continue;
+        const float G = gs_expf(power);
+        const float alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, G));
+        if (alpha < GS_ALPHA_MIN) continue;
+        any = true;
+        const float ra = __fdividef(1.0f, 1.0f - alpha);
+        T[p] *= ra;
+        const float aT = alpha * T[p];
         float dL_dalpha = 0.0f;
 #pragma unroll
         for (int ch = 0; ch < CMAX; ++ch) {
           const float c = s_col[ch][j];
-          accum[ch] = last_alpha * last_color[ch] + (1.0f - last_alpha) * accum[ch];
-          last_color[ch] = c;
-          dL_dalpha += (c - accum[ch]) * dpix[ch];
-          gv[6 + ch] = aT * dpix[ch];
+          accum[p][ch] = last_alpha[p] * last_color[p][ch] + (1.0f - last_alpha[p]) * accum[p][ch];
+          last_color[p][ch] = c;
+          dL_dalpha += (c - accum[p][ch]) * dpix[p][ch];
+          gv[6 + ch] += aT * dpix[p][ch];
         }
-        last_alpha = alpha;
-        dL_dalpha *= T;
-        dL_dalpha += (-T_final / (1.0f - alpha)) * bg_dot;
+        last_alpha[p] = alpha;
+        dL_dalpha = dL_dalpha * T[p] - T_final[p] * ra * bg_dot[p];
         const float dL_dG = co.w * dL_dalpha;
         const float gdx = G * dx, gdy = G * dy;
-        gv[0] = -(gdx * co.x + gdy * co.y) * dL_dG;
-        gv[1] = -(gdy * co.z + gdx * co.y) * dL_dG;
-        gv[2] = -0.5f * gdx * dx * dL_dG;
-        gv[3] = -gdx * dy * dL_dG;
-        gv[4] = -0.5f * gdy * dy * dL_dG;
-        gv[5] = G * dL_dalpha;
+        gv[0] -= (gdx * co.x + gdy * co.y) * dL_dG;
+        gv[1] -= (gdy * co.z + gdx * co.y) * dL_dG;
+        gv[2] -= 0.5f * gdx * dx * dL_dG;
+        gv[3] -= gdx * dy * dL_dG;
+        gv[4] -= 0.5f * gdy * dy * dL_dG;
+        gv[5] += G * dL_dalpha;
       }
-      if (__any_sync(0xffffffffu, contrib)) {
+      if (!__any_sync(0xffffffffu, any)) continue;
 #pragma unroll
-        for (int k = 0; k < NG; ++k) {
-          if (k >= 6 + a.cc) break;
-          float v = gv[k];
+      for (int k8 = 0; k8 < NV8; k8 += 8) {
+        const float t = warp_reduce8(gv + k8, lane);
+        if ((lane & 3) == 0) {
+          const int idx = k8 + ((lane >> 4) & 1) * 4 + ((lane >> 3) & 1) * 2 + ((lane >> 2) & 1);
+          if (idx < 6 + a.cc) s_gw[warp][idx][j] = t;
+        }
+      }
 #pragma unroll
-          for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-          gv[k] = v;
-        }
-        if (lane == 0) {
-          for (int k = 0; k < 6 + a.cc; ++k) atomicAdd(&s_g[k][j], gv[k]);
-          s_hit[j] = 1;
-        }
+      for (int k = NV8; k < NV; ++k) {
+        if (k >= 6 + a.cc) break;
+        const float t = warp_sum(gv[k]);
+        if (lane == 0) s_gw[warp][k][j] = t;
       }
     }
     __syncthreads();
-    if (threadIdx.x < bs && s_hit[threadIdx.x]) {
-      const int gid = s_id[threadIdx.x];
-      atomicAdd(g.g_means2d + 2 * gid, s_g[0][threadIdx.x]);
-      atomicAdd(g.g_means2d + 2 * gid + 1, s_g[1][threadIdx.x]);
-      atomicAdd(g.g_conics + 3 * gid, s_g[2][threadIdx.x]);
-      atomicAdd(g.g_conics + 3 * gid + 1, s_g[3][threadIdx.x]);
-      atomicAdd(g.g_conics + 3 * gid + 2, s_g[4][threadIdx.x]);
-      atomicAdd(g.g_opac + gid, s_g[5][threadIdx.x]);
-      for (int ch = 0; ch < a.cc; ++ch)
-        atomicAdd(g.g_colors + (int64_t)gid * a.c_total + a.c0 + ch, s_g[6 + ch][threadIdx.x]);
+    if (threadIdx.x < bs) {
+      const int t = threadIdx.x;
+      float tot[NV];
+      bool hit = false;
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        float v = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kBwdWarps; ++w) v += s_gw[w][k][t];
+        tot[k] = v;
+        hit |= v != 0.0f;
+      }
+      if (hit) {
+        const int gid = s_id[t];
+        atomicAdd(reinterpret_cast<float2*>(g.g_means2d) + gid, make_float2(tot[0], tot[1]));
+        atomicAdd(g.g_conics + 3 * gid, tot[2]);
+        atomicAdd(g.g_conics + 3 * gid + 1, tot[3]);
+        atomicAdd(g.g_conics + 3 * gid + 2, tot[4]);
+        atomicAdd(g.g_opac + gid, tot[5]);
+#pragma unroll
+        for (int ch = 0; ch < CMAX; ++ch)
+          if (ch < a.cc) atomicAdd(g.g_colors + (int64_t)gid * a.c_total + a.c0 + ch, tot[6 + ch]);
+      }
     }
   }
 }
@@ -292,9 +444,9 @@ constexpr int kMaxChunk = 16;
 template <int CMAX>
 static void launch_fwd(const RasterArgs& a, bool depth, int grid, cudaStream_t s) {
   if (depth)
-    k_raster_fwd<CMAX, true><<<grid, GS_BLOCK, 0, s>>>(a);
+    k_raster_fwd<CMAX, true><<<grid, kFwdThreads, 0, s>>>(a);
   else
-    k_raster_fwd<CMAX, false><<<grid, GS_BLOCK, 0, s>>>(a);
+    k_raster_fwd<CMAX, false><<<grid, kFwdThreads, 0, s>>>(a);
 }
 
 static void dispatch_fwd(const RasterArgs& a, bool depth, int grid, cudaStream_t s) {
@@ -311,12 +463,12 @@ static void dispatch_fwd(const RasterArgs& a, bool depth, int grid, cudaStream_t
 
 static void dispatch_bwd(const RasterBwdArgs& g, int grid, cudaStream_t s) {
   switch (pick_cmax(g.f.cc)) {
-    case 1: k_raster_bwd<1><<<grid, GS_BLOCK, 0, s>>>(g); break;
-    case 2: k_raster_bwd<2><<<grid, GS_BLOCK, 0, s>>>(g); break;
-    case 3: k_raster_bwd<3><<<grid, GS_BLOCK, 0, s>>>(g); break;
-    case 4: k_raster_bwd<4><<<grid, GS_BLOCK, 0, s>>>(g); break;
-    case 8: k_raster_bwd<8><<<grid, GS_BLOCK, 0, s>>>(g); break;
-    default: k_raster_bwd<16><<<grid, GS_BLOCK, 0, s>>>(g); break;
+    case 1: k_raster_bwd<1><<<grid, kBwdThreads, 0, s>>>(g); break;
+    case 2: k_raster_bwd<2><<<grid, kBwdThreads, 0, s>>>(g); break;
+    case 3: k_raster_bwd<3><<<grid, kBwdThreads, 0, s>>>(g); break;
+    case 4: k_raster_bwd<4><<<grid, kBwdThreads, 0, s>>>(g); break;
+    case 8: k_raster_bwd<8><<<grid, kBwdThreads, 0, s>>>(g); break;
+    default: k_raster_bwd<16><<<grid, kBwdThreads, 0, s>>>(g); break;
   }
 }
 
@@ -344,10 +496,12 @@ int gs_rasterize_forward(const float* means2d, const float* conics, const float*
                          float* depth, void* stream) {
   clear_error();
   if (int e = check_raster_args(channels, width, height, tiles_x, tiles_y)) return e;
-  if (!means2d || !conics || !opacities || !sorted_ids || !tile_ranges || !final_T)
-    return set_error(GS_ERR_INVALID_ARG, "gs_rasterize_forward: NULL pointer");
-  if (channels > 0 && (!colors || !image))
-    return set_error(GS_ERR_INVALID_ARG, "colors / image must be given when channels > 0");
+  // Per-Gaussian inputs may be NULL only when every tile range is empty
+  // (a scene with no Gaussians).
+  if (!tile_ranges || !final_T)
+    return set_error(GS_ERR_INVALID_ARG, "gs_rasterize_forward: NULL tile_ranges / final_T");
+  if (channels > 0 && !image)
+    return set_error(GS_ERR_INVALID_ARG, "image must be given when channels > 0");
   if (depth && !depths) return set_error(GS_ERR_INVALID_ARG, "depth output needs depths");
   if (!aligned(means2d, 8)) return set_error(GS_ERR_INVALID_ARG, "means2d must be 8-byte aligned");
   cudaStream_t s = as_stream(stream);
@@ -384,10 +538,12 @@ int gs_rasterize_backward(const float* means2d, const float* conics, const float
   clear_error();
   if (int e = check_raster_args(channels, width, height, tiles_x, tiles_y)) return e;
   if (channels < 1) return set_error(GS_ERR_INVALID_ARG, "backward needs channels >= 1");
+  if (n == 0) return GS_OK;  // no Gaussians, no gradients
   if (!means2d || !conics || !colors || !opacities || !sorted_ids || !tile_ranges || !final_T ||
       !n_contrib || !grad_image || !grad_means2d || !grad_conics || !grad_colors || !grad_opacities)
     return set_error(GS_ERR_INVALID_ARG, "gs_rasterize_backward: NULL pointer");
-  if (!aligned(means2d, 8)) return set_error(GS_ERR_INVALID_ARG, "means2d must be 8-byte aligned");
+  if (!aligned(means2d, 8) || !aligned(grad_means2d, 8))
+    return set_error(GS_ERR_INVALID_ARG, "means2d / grad_means2d must be 8-byte aligned");
   cudaStream_t s = as_stream(stream);
   if (n > 0) {
     bool ok = cudaMemsetAsync(grad_means2d, 0, sizeof(float) * 2 * n, s) == cudaSuccess &&

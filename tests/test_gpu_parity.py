@@ -152,7 +152,8 @@ def test_project_backward_matches_autodiff(aa):
             "compensation": rng.normal(size=n)}
     m, q, s = cu(means).requires_grad_(), cu(quats).requires_grad_(), cu(scales).requires_grad_()
     out = gs.project_gaussians(cam, m, q, s, antialias=aa)
-    keys = ["means2d", "conics", "depths", "compensation"]
+    # compensation is a constant (no gradient) unless antialias is on
+    keys = ["means2d", "conics", "depths"] + (["compensation"] if aa else [])
     torch.autograd.backward([out[k] for k in keys], [cu(cots[k]) for k in keys])
     tm, tq, ts = (torch.tensor(a, dtype=torch.float64, requires_grad=True) for a in (means, quats, scales))
     ref = torch_ref.project(cam, tm, tq, ts, antialias=aa)
@@ -338,3 +339,35 @@ def test_full_size_c2_properties():
     g2 = torch.autograd.grad(img, list(params.values()), 2.0 * g)
     for a, b in zip(g1, g2):
         assert rel_l2(npy(b), 2.0 * npy(a)) < 1e-5
+
+
+def test_full_size_c2_forward_bit_exact_and_gradients():
+    """The benchmark workload itself (1M Gaussians, SH3, 1080p, antialias)
+    against the oracle: forward bit-exact, gradients within 1e-4."""
+    sc = make_scene(2)
+    cam = sc.cameras[0]
+    params = sc.torch_params(requires_grad=True)
+    model = gs.GaussianModel(params, sh_degree=3)
+    model.active_sh_degree = 3
+    out = model.render(cam, antialias=True)
+    means, quats, scales, opac, sh = activated(sc)
+    fwd = orc.render(cam.to_native(), cam.width, cam.height, means, quats, scales, opac, sh=sh, sh_degree=3,
+                     antialias=True)
+    for k in ("radii", "image", "final_T", "n_contrib"):
+        eq(npy(out[k]), fwd[k], k)
+    rng = np.random.default_rng(21)
+    g_img = rng.normal(size=(cam.height, cam.width, 3)).astype(np.float32)
+    out["image"].backward(cu(g_img))
+    _, g = orc.render_grads(cam, means, quats, scales, opac, sh=sh, sh_degree=3, antialias=True, grad_image=g_img,
+                            fwd=fwd)
+    s_act, o_act = scales, opac
+    checks = {
+        "means": (params["means"].grad, g["means"]),
+        "quats": (params["quats"].grad, g["quats"]),
+        "scales": (params["scales"].grad, g["scales"] * s_act),
+        "opacities": (params["opacities"].grad, g["opacities"] * o_act * (1 - o_act)),
+        "sh_dc": (params["sh_dc"].grad, g["sh"][:, :1]),
+        "sh_rest": (params["sh_rest"].grad, g["sh"][:, 1:]),
+    }
+    for k, (a, b) in checks.items():
+        assert rel_l2(npy(a), b) < GRAD_TOL, k
