@@ -145,7 +145,10 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
     const int bs = min(kFwdBatch, num - b0);
     for (int j = 0; j < bs; ++j) {
       if (done[0] && done[1]) break;
-      if (tp.misses(s_bb[j])) continue;
+      const float4 bb = s_bb[j];
+      // Whole-warp skip only: a per-pixel box test saves nothing under SIMT
+      // unless every lane skips, which this test already catches.
+      if (tp.misses(bb)) continue;
       const float2 m = s_xy[j];
       const float4 co = s_co[j];
       const float pf = s_pf[j];
@@ -277,32 +280,37 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
   const int start = a.ranges[2 * tile], end = a.ranges[2 * tile + 1];
   const int num = end - start;
 
+  // Per-pixel state of the back-to-front replay.  The reference keeps the
+  // colour composited behind the current Gaussian, accum (rasterize.py:183),
+  // and uses (c - accum) . dL/dpix * T.  Since T_i * accum_i . dL/dpix =
+  // R_i / (1 - alpha_i) with R_i = sum_{j > i} (c_j . dL/dpix) alpha_j T_j,
+  // one scalar R per pixel carries the same information.
+  // tail = T_final * (bg . dL/dpix + dL/dT_final), the background term.
   bool inside[2];
-  float pyf[2], T[2], T_final[2], bg_dot[2], last_alpha[2];
+  float pyf[2], T[2], R[2], tail[2];
   int last[2];
-  float dpix[2][CMAX], accum[2][CMAX], last_color[2][CMAX];
+  float dpix[2][CMAX];
 #pragma unroll
   for (int p = 0; p < 2; ++p) {
     const int py = py0 + p;
     inside[p] = px < a.width && py < a.height;
     pyf[p] = (float)py + 0.5f;
     const int64_t pid = (int64_t)py * a.width + px;
-    T_final[p] = inside[p] ? a.final_T[pid] : 1.0f;
-    T[p] = T_final[p];
+    const float T_final = inside[p] ? a.final_T[pid] : 1.0f;
+    T[p] = T_final;
+    R[p] = 0.0f;
     last[p] = inside[p] ? a.n_contrib[pid] : 0;
-    bg_dot[p] = 0.0f;
-    last_alpha[p] = 0.0f;
+    float bg_dot = 0.0f;
 #pragma unroll
     for (int ch = 0; ch < CMAX; ++ch) {
       dpix[p][ch] = 0.0f;
-      accum[p][ch] = 0.0f;
-      last_color[p][ch] = 0.0f;
       if (inside[p] && ch < a.cc) {
         dpix[p][ch] = g.grad_image[pid * a.c_total + a.c0 + ch];
-        if (a.bg) bg_dot[p] += a.bg[a.c0 + ch] * dpix[p][ch];
+        if (a.bg) bg_dot += a.bg[a.c0 + ch] * dpix[p][ch];
       }
     }
-    if (inside[p] && g.use_grad_final_T && g.grad_final_T) bg_dot[p] += g.grad_final_T[pid];
+    if (inside[p] && g.use_grad_final_T && g.grad_final_T) bg_dot += g.grad_final_T[pid];
+    tail[p] = T_final * bg_dot;
   }
 
   // Nothing at or beyond the largest n_contrib of a warp (block) matters.
@@ -343,7 +351,9 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
     const int bs = min(BATCH, num - b0);
     const int jtop = min(bs, wmax - b0) - 1;
     for (int j = jtop; j >= 0; --j) {
-      if (tp.misses(s_bb[j])) continue;
+      const float4 bb = s_bb[j];
+      if (tp.misses(bb)) continue;  // the whole warp's quadrant is outside the box
+      const bool col_in = pxf >= bb.x && pxf <= bb.y;
       const float4 co = s_co[j];
       const float2 m = s_xy[j];
       const float pf = s_pf[j];
@@ -353,7 +363,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
       bool any = false;
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        if (!(inside[p] && b0 + j < last[p])) continue;
+        if (!(col_in && b0 + j < last[p] && pyf[p] >= bb.z && pyf[p] <= bb.w)) continue;
         const float dx = gs_sub(m.x, pxf), dy = gs_sub(m.y, pyf[p]);
         const float power = gs_sub(
             gs_mul(-0.5f, gs_add(gs_mul(gs_mul(co.x, dx), dx), gs_mul(gs_mul(co.z, dy), dy))),
@@ -366,17 +376,14 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         const float ra = __fdividef(1.0f, 1.0f - alpha);
         T[p] *= ra;
         const float aT = alpha * T[p];
-        float dL_dalpha = 0.0f;
+        float cd = 0.0f;  // c . dL/dpix
 #pragma unroll
         for (int ch = 0; ch < CMAX; ++ch) {
-          const float c = s_col[ch][j];
-          accum[p][ch] = last_alpha[p] * last_color[p][ch] + (1.0f - last_alpha[p]) * accum[p][ch];
-          last_color[p][ch] = c;
-          dL_dalpha += (c - accum[p][ch]) * dpix[p][ch];
+          cd += s_col[ch][j] * dpix[p][ch];
           gv[6 + ch] += aT * dpix[p][ch];
         }
-        last_alpha[p] = alpha;
-        dL_dalpha = dL_dalpha * T[p] - T_final[p] * ra * bg_dot[p];
+        const float dL_dalpha = T[p] * cd - (R[p] + tail[p]) * ra;
+        R[p] += cd * aT;
         const float dL_dG = co.w * dL_dalpha;
         const float gdx = G * dx, gdy = G * dy;
         gv[0] -= (gdx * co.x + gdy * co.y) * dL_dG;
