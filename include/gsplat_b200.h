@@ -158,6 +158,26 @@ int gs_bin_end(const float* means2d, const float* radii, int64_t n, int64_t d, i
                int height, void* ws_n, size_t ws_n_bytes, void* ws_d, size_t ws_d_bytes,
                int32_t* sorted_ids, int32_t* tile_ranges, void* stream);
 
+/* No-allocation binning.  Has no counterpart in the reference: it exists
+ * for callers that cannot allocate device memory (a renderer embedded in an
+ * application whose GPU memory belongs to another allocator, a plugin host,
+ * a fixed-pool server).  Same results as gs_tile_counts + gs_bin_begin +
+ * gs_bin_end, with all scratch space in one file-scope __device__ array of
+ * GS_STATIC_BIN_SCRATCH_BYTES (20 MiB) that every GPU loading this library
+ * holds until process exit.  Limits: n <= GS_STATIC_BIN_MAX_N,
+ * D <= GS_STATIC_BIN_MAX_D; larger sizes return GS_ERR_CAPACITY, as does a
+ * sorted_ids capacity below D (*d_out then holds the D needed).  Reads D back
+ * to the host (one synchronisation of `stream`).  The first call on a device
+ * looks up the array's device address: make it before any stream capture.
+ * All calls share the array; calls that overlap on the GPU race. */
+#define GS_STATIC_BIN_MAX_N 131072
+#define GS_STATIC_BIN_MAX_D 1048576
+#define GS_STATIC_BIN_SCRATCH_BYTES (20u << 20)
+int gs_bin_gaussians_static(const float* means2d, const float* radii, const float* depths,
+                            int64_t n, int width, int height, int64_t d_capacity,
+                            int32_t* sorted_ids, int32_t* tile_ranges, int64_t* d_out,
+                            void* stream);
+
 /* --------------------------------------------------------------- compositing
  * Forward tile compositor (gs_rasterize_forward Metal kernel,
  * src/mlx3d/splatting/rasterize.py:28-98, 345-361, and the depth kernel
