@@ -269,7 +269,7 @@ def run_ours(args, world, rank, local):
         for k, v in sorted(stages.items(), key=lambda kv: -kv[1])
     }
     traffic = None
-    tf = ROOT / "profiles" / "traffic.json"
+    tf = ROOT / "profiles" / "dram_traffic_c2.json"
     if tf.exists():
         traffic = json.loads(tf.read_text()).get(dom)
 
