@@ -24,7 +24,7 @@ namespace gs {
 
 constexpr int RS_THREADS = 256;
 constexpr int RS_WARPS = RS_THREADS / 32;
-constexpr int RS_ITEMS = 16;
+constexpr int RS_ITEMS = 8;
 constexpr int RS_TILE = RS_THREADS * RS_ITEMS;  // keys per block
 constexpr int RS_RADIX = 256;
 constexpr int DEPTH_PASSES = 4;

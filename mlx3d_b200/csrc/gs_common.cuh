@@ -31,14 +31,50 @@ inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }
 
-// Cooperative copy of `rows` rows of `row_len` floats (source row stride
-// `stride` floats) into shared memory with row pitch `ld`.  Consecutive
-// threads read consecutive floats of the flattened chunk, so global loads are
-// coalesced whatever the row width.
+// ------------------------------------------------ row staging through smem
+// A block of `rows` consecutive rows of `row_len` floats (row stride `stride`
+// floats) is copied into shared memory so that every global access is
+// coalesced.  When the block is one contiguous, 16-byte-aligned chunk and the
+// row length is odd, it is copied with 16-byte cp.async transfers (many in
+// flight per thread) into an unpadded buffer (pitch = row_len; odd pitches
+// make "thread i reads row i" conflict-free); otherwise with scalar loads
+// into a buffer of odd pitch row_len | 1.
+
+__device__ __forceinline__ bool rows_contiguous(const float* g, int64_t stride, int row_len) {
+  return stride == row_len && (row_len & 1) && (reinterpret_cast<uintptr_t>(g) & 15) == 0;
+}
+
+// Shared-memory pitch stage_rows uses for this row block.
+__device__ __forceinline__ int stage_pitch(const float* g, int64_t stride, int row_len) {
+  return rows_contiguous(g, stride, row_len) ? row_len : (row_len | 1);
+}
+
+__device__ __forceinline__ void cp_async16(float* smem_dst, const float* gsrc) {
+  const unsigned s = (unsigned)__cvta_generic_to_shared(smem_dst);
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gsrc) : "memory");
+}
+
+// Completes every cp.async this thread issued; follow with __syncthreads().
+__device__ __forceinline__ void cp_async_wait_all() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+  asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+}
+
+// Issues the copy of a row block into `dst` (16-byte aligned, pitch
+// stage_pitch(...)).  Call cp_async_wait_all() and __syncthreads() before
+// reading it.
 template <int BLK>
-__device__ __forceinline__ void stage_rows(float* dst, int ld, const float* __restrict__ src,
-                                           int64_t stride, int row_len, int rows) {
+__device__ __forceinline__ void stage_rows(float* dst, const float* __restrict__ src, int64_t stride,
+                                           int row_len, int rows) {
   const int total = rows * row_len;
+  if (rows_contiguous(src, stride, row_len)) {
+    const int nv = total >> 2;
+    for (int v = threadIdx.x; v < nv; v += BLK) cp_async16(dst + 4 * v, src + 4 * v);
+    for (int e = (nv << 2) + threadIdx.x; e < total; e += BLK) dst[e] = __ldg(src + e);
+    return;
+  }
+  const int ld = row_len | 1;
+#pragma unroll 4
   for (int e = threadIdx.x; e < total; e += BLK) {
     const int row = e / row_len;
     const int col = e - row * row_len;
@@ -46,11 +82,19 @@ __device__ __forceinline__ void stage_rows(float* dst, int ld, const float* __re
   }
 }
 
-// Inverse of stage_rows: coalesced write-back of a shared-memory row block.
+// Coalesced write-back of a shared-memory row block of pitch `ld` to global
+// rows of stride `stride` (vector stores when both sides allow it).
 template <int BLK>
 __device__ __forceinline__ void unstage_rows(float* __restrict__ dst, int64_t stride,
                                              const float* src, int ld, int row_len, int rows) {
   const int total = rows * row_len;
+  if (ld == row_len && rows_contiguous(dst, stride, row_len)) {
+    const int nv = total >> 2;
+    for (int v = threadIdx.x; v < nv; v += BLK)
+      reinterpret_cast<float4*>(dst)[v] = reinterpret_cast<const float4*>(src)[v];
+    for (int e = (nv << 2) + threadIdx.x; e < total; e += BLK) dst[e] = src[e];
+    return;
+  }
   for (int e = threadIdx.x; e < total; e += BLK) {
     const int row = e / row_len;
     const int col = e - row * row_len;

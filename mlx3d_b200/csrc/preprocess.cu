@@ -212,44 +212,42 @@ struct PreFwdArgs {
 
 constexpr int kPreBlock = 128;
 
-// Shared-memory layout of one block's staged rows (row pitch odd => no bank
-// conflicts when thread i reads row i).
-struct PreSmem {
-  int rest_len, rest_ld;
-  __device__ static int pitch(int len) { return len | 1; }
-};
-
 __global__ void __launch_bounds__(kPreBlock) k_preprocess_fwd(const PreFwdArgs a) {
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   const int64_t base = (int64_t)blockIdx.x * kPreBlock;
   const int rows = (int)min((int64_t)kPreBlock, a.n - base);
   const int nb = a.sh_degree >= 0 ? (a.sh_degree + 1) * (a.sh_degree + 1) : 0;
   const int rest_len = nb > 1 ? (nb - 1) * 3 : 0;
-  const int rest_ld = PreSmem::pitch(rest_len);
-  float* s_means = smem;                       // 3
-  float* s_scales = s_means + kPreBlock * 3;   // 3
-  float* s_dc = s_scales + kPreBlock * 3;      // 3
-  float* s_rest = s_dc + kPreBlock * 3;        // rest_ld
-  stage_rows<kPreBlock>(s_means, 3, a.means + base * 3, 3, 3, rows);
-  stage_rows<kPreBlock>(s_scales, 3, a.scales + base * 3, 3, 3, rows);
+  const float* g_means = a.means + base * 3;
+  const float* g_scales = a.scales + base * 3;
+  const float* g_dc = a.sh_dc ? a.sh_dc + base * a.dc_stride : nullptr;
+  const float* g_rest = a.sh_rest ? a.sh_rest + base * a.rest_stride : nullptr;
+  const int mld = stage_pitch(g_means, 3, 3), sld = stage_pitch(g_scales, 3, 3);
+  const int dld = g_dc ? stage_pitch(g_dc, a.dc_stride, 3) : 3;
+  const int rest_ld = rest_len ? stage_pitch(g_rest, a.rest_stride, rest_len) : 1;
+  float* s_means = smem;                       // pitch <= 4
+  float* s_scales = s_means + kPreBlock * 4;   // pitch <= 4
+  float* s_dc = s_scales + kPreBlock * 4;      // pitch <= 4
+  float* s_rest = s_dc + kPreBlock * 4;        // pitch <= rest_len | 1
+  stage_rows<kPreBlock>(s_means, g_means, 3, 3, rows);
+  stage_rows<kPreBlock>(s_scales, g_scales, 3, 3, rows);
   if (a.fused && nb > 0) {
-    stage_rows<kPreBlock>(s_dc, 3, a.sh_dc + base * a.dc_stride, a.dc_stride, 3, rows);
-    if (rest_len > 0)
-      stage_rows<kPreBlock>(s_rest, rest_ld, a.sh_rest + base * a.rest_stride, a.rest_stride,
-                            rest_len, rows);
+    stage_rows<kPreBlock>(s_dc, g_dc, a.dc_stride, 3, rows);
+    if (rest_len > 0) stage_rows<kPreBlock>(s_rest, g_rest, a.rest_stride, rest_len, rows);
   }
+  cp_async_wait_all();
   __syncthreads();
   const int li = threadIdx.x;
   if (li >= rows) return;
   const int64_t i = base + li;
   const float4 q = __ldg(reinterpret_cast<const float4*>(a.quats) + i);
-  float s0 = s_scales[li * 3 + 0], s1 = s_scales[li * 3 + 1], s2 = s_scales[li * 3 + 2];
+  float s0 = s_scales[li * sld + 0], s1 = s_scales[li * sld + 1], s2 = s_scales[li * sld + 2];
   if (a.flags & GS_ACT_EXP_SCALES) {
     s0 = gs_expf(s0);
     s1 = gs_expf(s1);
     s2 = gs_expf(s2);
   }
-  const float m0 = s_means[li * 3 + 0], m1 = s_means[li * 3 + 1], m2 = s_means[li * 3 + 2];
+  const float m0 = s_means[li * mld + 0], m1 = s_means[li * mld + 1], m2 = s_means[li * mld + 2];
   Proj p;
   project_one(a.cam, m0, m1, m2, q.x, q.y, q.z, q.w, s0, s1, s2, a.blur, a.aa != 0, p);
   reinterpret_cast<float2*>(a.means2d)[i] = make_float2(p.u, p.v);
@@ -273,7 +271,7 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_fwd(const PreFwdArgs a
     sh_basis(a.sh_degree, dx, dy, dz, bs);
 #pragma unroll
     for (int ch = 0; ch < 3; ++ch) {
-      float r = gs_mul(bs[0], s_dc[li * 3 + ch]);
+      float r = gs_mul(bs[0], s_dc[li * dld + ch]);
       for (int k = 1; k < nb; ++k) r = gs_add(r, gs_mul(bs[k], s_rest[li * rest_ld + (k - 1) * 3 + ch]));
       r = gs_add(r, 0.5f);
       a.colors[i * 3 + ch] = gs_maxf(r, 0.0f);
@@ -413,32 +411,44 @@ __device__ __forceinline__ void project_vjp(const gs_camera& cam, float m0, floa
 }
 
 __global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd(const PreBwdArgs g) {
-  extern __shared__ float smem[];
+  extern __shared__ __align__(16) float smem[];
   const PreFwdArgs& a = g.f;
   const int64_t base = (int64_t)blockIdx.x * kPreBlock;
   const int rows = (int)min((int64_t)kPreBlock, a.n - base);
   const int nb = a.sh_degree >= 0 ? (a.sh_degree + 1) * (a.sh_degree + 1) : 0;
   const int rest_len = nb > 1 ? (nb - 1) * 3 : 0;
-  const int rest_ld = PreSmem::pitch(rest_len);
+  const bool sh = a.fused && nb > 0;
+  const float* g_means = a.means + base * 3;
+  const float* g_scales = a.scales + base * 3;
+  const float* g_dc = sh ? a.sh_dc + base * a.dc_stride : nullptr;
+  const float* g_rest = (sh && rest_len) ? a.sh_rest + base * a.rest_stride : nullptr;
+  const int mld = stage_pitch(g_means, 3, 3), sld = stage_pitch(g_scales, 3, 3);
+  const int dld = g_dc ? stage_pitch(g_dc, a.dc_stride, 3) : 3;
+  const int rest_ld = g_rest ? stage_pitch(g_rest, a.rest_stride, rest_len) : 1;
   float* s_means = smem;
-  float* s_scales = s_means + kPreBlock * 3;
-  float* s_dc = s_scales + kPreBlock * 3;      // gradient rows of sh_dc
-  float* s_rest = s_dc + kPreBlock * 3;        // gradient rows of sh_rest
-  stage_rows<kPreBlock>(s_means, 3, a.means + base * 3, 3, 3, rows);
-  stage_rows<kPreBlock>(s_scales, 3, a.scales + base * 3, 3, 3, rows);
+  float* s_scales = s_means + kPreBlock * 4;
+  float* s_dc = s_scales + kPreBlock * 4;      // sh_dc rows, then their gradients
+  float* s_rest = s_dc + kPreBlock * 4;        // sh_rest rows, then their gradients
+  stage_rows<kPreBlock>(s_means, g_means, 3, 3, rows);
+  stage_rows<kPreBlock>(s_scales, g_scales, 3, 3, rows);
+  if (sh) {
+    stage_rows<kPreBlock>(s_dc, g_dc, a.dc_stride, 3, rows);
+    if (g_rest) stage_rows<kPreBlock>(s_rest, g_rest, a.rest_stride, rest_len, rows);
+  }
+  cp_async_wait_all();
   __syncthreads();
   const int li = threadIdx.x;
   if (li < rows) {
     const int64_t i = base + li;
     const float4 q = __ldg(reinterpret_cast<const float4*>(a.quats) + i);
-    const float r0 = s_scales[li * 3 + 0], r1 = s_scales[li * 3 + 1], r2 = s_scales[li * 3 + 2];
+    const float r0 = s_scales[li * sld + 0], r1 = s_scales[li * sld + 1], r2 = s_scales[li * sld + 2];
     float s0 = r0, s1 = r1, s2 = r2;
     if (a.flags & GS_ACT_EXP_SCALES) {
       s0 = gs_expf(r0);
       s1 = gs_expf(r1);
       s2 = gs_expf(r2);
     }
-    const float m0 = s_means[li * 3 + 0], m1 = s_means[li * 3 + 1], m2 = s_means[li * 3 + 2];
+    const float m0 = s_means[li * mld + 0], m1 = s_means[li * mld + 1], m2 = s_means[li * mld + 2];
     float gu = 0.f, gv = 0.f, gA = 0.f, gB = 0.f, gC = 0.f, gz = 0.f, gcomp = 0.f;
     if (g.g_means2d) { gu = g.g_means2d[2 * i]; gv = g.g_means2d[2 * i + 1]; }
     if (g.g_conics) { gA = g.g_conics[3 * i]; gB = g.g_conics[3 * i + 1]; gC = g.g_conics[3 * i + 2]; }
@@ -473,28 +483,28 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd(const PreBwdArgs g
     g.g_scales[3 * i + 0] = gsc[0];
     g.g_scales[3 * i + 1] = gsc[1];
     g.g_scales[3 * i + 2] = gsc[2];
-    if (a.fused && nb > 0) {
-      // colors = max(eval_sh(...), 0): recompute the raw value to mask.
+    if (sh) {
+      // colors = max(eval_sh(...), 0): recompute the raw value to mask the
+      // gradient, then overwrite the staged coefficients with their gradients
+      // (each channel's coefficients are read before they are overwritten).
       float dx, dy, dz;
       view_dir(a.cam, m0, m1, m2, dx, dy, dz);
       float bs[16];
       sh_basis(a.sh_degree, dx, dy, dz, bs);
-      const float* dc = a.sh_dc + i * a.dc_stride;
-      const float* rest = a.sh_rest + i * a.rest_stride;
 #pragma unroll
       for (int ch = 0; ch < 3; ++ch) {
-        float r = gs_mul(bs[0], __ldg(dc + ch));
-        for (int k = 1; k < nb; ++k) r = gs_add(r, gs_mul(bs[k], __ldg(rest + (k - 1) * 3 + ch)));
+        float r = gs_mul(bs[0], s_dc[li * dld + ch]);
+        for (int k = 1; k < nb; ++k) r = gs_add(r, gs_mul(bs[k], s_rest[li * rest_ld + (k - 1) * 3 + ch]));
         r = gs_add(r, 0.5f);
         const float gcol = r > 0.0f ? g.g_colors[3 * i + ch] : 0.0f;
-        s_dc[li * 3 + ch] = bs[0] * gcol;
+        s_dc[li * dld + ch] = bs[0] * gcol;
         for (int k = 1; k < nb; ++k) s_rest[li * rest_ld + (k - 1) * 3 + ch] = bs[k] * gcol;
       }
     }
   }
-  if (a.fused && nb > 0) {
+  if (sh) {
     __syncthreads();
-    unstage_rows<kPreBlock>(g.g_sh_dc + base * a.dc_stride, a.dc_stride, s_dc, 3, 3, rows);
+    unstage_rows<kPreBlock>(g.g_sh_dc + base * a.dc_stride, a.dc_stride, s_dc, dld, 3, rows);
     if (rest_len > 0)
       unstage_rows<kPreBlock>(g.g_sh_rest + base * a.rest_stride, a.rest_stride, s_rest, rest_ld,
                               rest_len, rows);
@@ -562,7 +572,7 @@ __global__ void k_tile_counts(const float* __restrict__ means2d, const float* __
 static size_t pre_smem_bytes(int sh_degree, bool fused) {
   const int nb = (fused && sh_degree >= 0) ? (sh_degree + 1) * (sh_degree + 1) : 0;
   const int rest_len = nb > 1 ? (nb - 1) * 3 : 0;
-  return sizeof(float) * (size_t)kPreBlock * (3 + 3 + 3 + (rest_len | 1));
+  return sizeof(float) * (size_t)kPreBlock * (4 + 4 + 4 + (rest_len | 1));
 }
 
 static int check_cam(const gs_camera* cam) {
