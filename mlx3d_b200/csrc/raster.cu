@@ -73,6 +73,49 @@ struct TilePixels {
   }
 };
 
+// Minimum over the rectangle [x0,x1] x [y0,y1] of the positive-definite
+// form A dx^2 + 2 B dx dy + C dy^2: 0 if the rectangle contains the origin,
+// else the smallest of the four edge minima, each at the edge's clipped 1-D
+// minimiser (the corner-and-edge evaluation of the reference's tile
+// refinement, tiles.py:113-139).
+__device__ __forceinline__ float rect_qmin(float A, float B, float C, float rbc, float rba, float x0,
+                                           float x1, float y0, float y1) {
+  if (x0 <= 0.0f && x1 >= 0.0f && y0 <= 0.0f && y1 >= 0.0f) return 0.0f;
+  auto q = [&](float dx, float dy) { return A * dx * dx + 2.0f * B * dx * dy + C * dy * dy; };
+  const float m0 = q(x0, fminf(fmaxf(-rbc * x0, y0), y1));
+  const float m1 = q(x1, fminf(fmaxf(-rbc * x1, y0), y1));
+  const float m2 = q(fminf(fmaxf(-rba * y0, x0), x1), y0);
+  const float m3 = q(fminf(fmaxf(-rba * y1, x0), x1), y1);
+  return fminf(fminf(m0, m1), fminf(m2, m3));
+}
+
+// Bit w set: warp w's 8x8 quadrant of tile `tile` may hold a pixel with
+// power >= pf.  A quadrant is dropped only when its pixel-centre rectangle,
+// widened by 1 px, lies outside the ellipse q <= 2 (1.05 L + 0.05),
+// L = -pf — margins far above the float32 error of power near the ellipse
+// (the same safety argument as cull_box, which it refines).
+__device__ __forceinline__ int quad_mask(float2 m, float4 co, float pf, float4 bb, int tile,
+                                         int tiles_x) {
+  const float L = -pf;
+  if (!(L > 0.0f)) return 0;
+  const float det = co.x * co.z - co.y * co.y;
+  if (!(det > 0.0f) || !(co.x > 0.0f) || !(co.z > 0.0f)) return 0xF;
+  const float lim = 2.0f * (1.05f * L + 0.05f);
+  const float rbc = __fdividef(co.y, co.z), rba = __fdividef(co.y, co.x);
+  const float tx0 = (float)((tile % tiles_x) * GS_TILE), ty0 = (float)((tile / tiles_x) * GS_TILE);
+  int mask = 0;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float qx = tx0 + (float)((w & 1) * 8), qy = ty0 + (float)((w >> 1) * 8);
+    // quadrant pixel centres span [q + 0.5, q + 7.5]; box test first (cheap)
+    if (bb.y < qx + 0.5f || bb.x > qx + 7.5f || bb.w < qy + 0.5f || bb.z > qy + 7.5f) continue;
+    const float v = rect_qmin(co.x, co.y, co.z, rbc, rba, qx - 0.5f - m.x, qx + 8.5f - m.x,
+                              qy - 0.5f - m.y, qy + 8.5f - m.y);
+    if (v <= lim) mask |= 1 << w;
+  }
+  return mask;
+}
+
 // Forward compositor.  One CTA of 128 threads per tile (TilePixels layout);
 // each thread owns two pixels, so every staged Gaussian is read from shared
 // memory once per two pixels, and a warp skips Gaussians whose cull_box
@@ -89,11 +132,12 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
   __shared__ float2 s_xy[kFwdBatch];
   __shared__ float4 s_co[kFwdBatch];  // conic a, b, c, opacity
   __shared__ float s_pf[kFwdBatch];   // power floor
-  __shared__ float4 s_bb[kFwdBatch];  // cull box
+  __shared__ int s_qm[kFwdBatch];     // quad_mask
   __shared__ float s_col[NC][kFwdBatch];
   __shared__ float s_z[DEPTH ? kFwdBatch : 1];
 
   const int tile = blockIdx.x;
+  const int warp = threadIdx.x >> 5;
   const TilePixels tp(tile, a.tiles_x);
   const int px = tp.px, py0 = tp.py0;
   const float pxf = (float)px + 0.5f;
@@ -134,7 +178,7 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
         s_xy[t] = m;
         s_co[t] = co;
         s_pf[t] = pf;
-        s_bb[t] = cull_box(m, co, pf);
+        s_qm[t] = quad_mask(m, co, pf, cull_box(m, co, pf), tile, a.tiles_x);
 #pragma unroll
         for (int ch = 0; ch < CMAX; ++ch)
           if (ch < a.cc) s_col[ch][t] = __ldg(a.colors + (int64_t)g * a.c_total + a.c0 + ch);
@@ -145,10 +189,9 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
     const int bs = min(kFwdBatch, num - b0);
     for (int j = 0; j < bs; ++j) {
       if (done[0] && done[1]) break;
-      const float4 bb = s_bb[j];
-      // Whole-warp skip only: a per-pixel box test saves nothing under SIMT
+      // Whole-warp skip only: a per-pixel test saves nothing under SIMT
       // unless every lane skips, which this test already catches.
-      if (tp.misses(bb)) continue;
+      if (!((s_qm[j] >> warp) & 1)) continue;
       const float2 m = s_xy[j];
       const float4 co = s_co[j];
       const float pf = s_pf[j];
@@ -266,6 +309,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
   __shared__ float4 s_co[BATCH];
   __shared__ float s_pf[BATCH];
   __shared__ float4 s_bb[BATCH];
+  __shared__ int s_qm[BATCH];
   __shared__ float s_col[CMAX][BATCH];
   // per-warp gradient totals; the +1 pitch puts the eight values a warp
   // stores for one Gaussian in eight different banks
@@ -339,7 +383,9 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         s_xy[threadIdx.x] = m;
         s_co[threadIdx.x] = co;
         s_pf[threadIdx.x] = pf;
-        s_bb[threadIdx.x] = cull_box(m, co, pf);
+        const float4 bb = cull_box(m, co, pf);
+        s_bb[threadIdx.x] = bb;
+        s_qm[threadIdx.x] = quad_mask(m, co, pf, bb, tile, a.tiles_x);
 #pragma unroll
         for (int ch = 0; ch < CMAX; ++ch)
           s_col[ch][threadIdx.x] =
@@ -351,8 +397,8 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
     const int bs = min(BATCH, num - b0);
     const int jtop = min(bs, wmax - b0) - 1;
     for (int j = jtop; j >= 0; --j) {
+      if (!((s_qm[j] >> warp) & 1)) continue;  // the whole warp's quadrant is outside
       const float4 bb = s_bb[j];
-      if (tp.misses(bb)) continue;  // the whole warp's quadrant is outside the box
       const bool col_in = pxf >= bb.x && pxf <= bb.y;
       const float4 co = s_co[j];
       const float2 m = s_xy[j];
