@@ -183,10 +183,10 @@ def run_ours(args, world, rank, local):
     target = scene.target(view=rank, device=dev)
     plist = list(params.values())
 
+    from mlx3d_b200.distributed import allreduce_gradients
+
     def allreduce_grads():
-        if world > 1:
-            for p in plist:
-                dist.all_reduce(p.grad)
+        allreduce_gradients(plist)
 
     def step():
         for p in plist:
@@ -270,7 +270,7 @@ def run_ours(args, world, rank, local):
     }
     traffic = None
     tf = ROOT / "profiles" / "dram_traffic_c2.json"
-    if tf.exists():
+    if tf.exists() and cfg.index == 2 and args.n is None:
         traffic = json.loads(tf.read_text()).get(dom)
 
     # ---- end to end through the public API with host buffers

@@ -1,0 +1,50 @@
+"""Data parallelism over camera views (one process per GPU).
+
+Views are independent until the per-Gaussian gradient sum, so a multi-view
+render or training step shards the views over ranks (view k goes to rank
+k mod world) and sums the gradients of the replicated Gaussian parameters
+with one all-reduce per parameter tensor — the only collective on this path.
+The reference has no multi-device code; this is the B200 build's addition.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+__all__ = ["shard_views", "allreduce_gradients", "world"]
+
+
+def world() -> tuple[int, int]:
+    """(rank, world size) of the default process group, (0, 1) without one."""
+    if dist.is_available() and dist.is_initialized():
+        return dist.get_rank(), dist.get_world_size()
+    return 0, 1
+
+
+def shard_views(views: list, rank: int | None = None, world_size: int | None = None) -> list:
+    """The views rank ``rank`` renders: every ``world_size``-th view starting at
+    ``rank`` (an even split when the count divides; otherwise the first ranks
+    get one more)."""
+    if rank is None or world_size is None:
+        rank, world_size = world()
+    if not 0 <= rank < world_size:
+        raise ValueError(f"rank {rank} outside world of size {world_size}")
+    return list(views[rank::world_size])
+
+
+def allreduce_gradients(params: dict[str, torch.Tensor] | list[torch.Tensor], average: bool = False,
+                        group=None) -> None:
+    """Sum (or average) ``.grad`` of every parameter over all ranks in place.
+    Parameters without a gradient contribute zeros (allocated here) so every
+    rank issues the same sequence of collectives."""
+    rank, ws = world()
+    if ws == 1:
+        return
+    tensors = list(params.values()) if isinstance(params, dict) else list(params)
+    for p in tensors:
+        if p.grad is None:
+            p.grad = torch.zeros_like(p)
+        dist.all_reduce(p.grad, op=dist.ReduceOp.SUM, group=group)
+        if average:
+            p.grad.div_(ws)

@@ -1,0 +1,63 @@
+"""View sharding and the gradient all-reduce with two gloo ranks on CPU."""
+
+import os
+import socket
+
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from mlx3d_b200.distributed import allreduce_gradients, shard_views
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _worker(rank, world_size, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world_size)
+    try:
+        views = list(range(7))
+        mine = shard_views(views)
+        params = {"means": torch.zeros(5, 3, requires_grad=True), "opacities": torch.zeros(5, requires_grad=True),
+                  "unused": torch.zeros(2, requires_grad=True)}
+        # each rank's gradient: the sum over its views of view-dependent values
+        params["means"].grad = torch.stack([torch.full((3,), float(v)) for v in range(5)]) * sum(mine)
+        params["opacities"].grad = torch.ones(5) * (rank + 1)
+        allreduce_gradients(params)
+        results[rank] = (mine, params["means"].grad.clone(), params["opacities"].grad.clone(),
+                         params["unused"].grad.clone())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_view_sharding_and_gradient_sum():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_worker, args=(r, 2, port, results)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+        r0, r1 = results[0], results[1]
+    assert r0[0] == [0, 2, 4, 6] and r1[0] == [1, 3, 5]
+    total = sum(range(7))
+    expect = torch.stack([torch.full((3,), float(v)) for v in range(5)]) * total
+    for r in (r0, r1):
+        torch.testing.assert_close(r[1], expect)
+        torch.testing.assert_close(r[2], torch.full((5,), 3.0))
+        torch.testing.assert_close(r[3], torch.zeros(2))
+
+
+def test_shard_views_validates_rank():
+    assert shard_views([1, 2, 3], 0, 1) == [1, 2, 3]
+    with pytest.raises(ValueError):
+        shard_views([1], 2, 2)
