@@ -205,6 +205,45 @@ int gs_rasterize_backward(const float* means2d, const float* conics, const float
                           float* grad_means2d, float* grad_conics, float* grad_colors,
                           float* grad_opacities, void* stream);
 
+/* ------------------------------------------------------------ training step
+ * Photometric loss of GaussianTrainer._render_loss
+ * (src/mlx3d/splatting/trainer.py:300-305): loss[0] = (1 - lambda) * L1 +
+ * lambda * (1 - SSIM), loss[1] = L1, loss[2] = SSIM, with SSIM as
+ * losses/image_metrics.py:29-85 (Gaussian window `window_size` / `sigma`,
+ * zero padding, constants (0.01 max_val)^2 and (0.03 max_val)^2, means over
+ * H*W*C).  pred / target (H, W, C); `loss` is a device float[3].  The
+ * forward leaves per-pixel SSIM partials in the workspace
+ * (gs_l1_ssim_workspace_bytes) for gs_l1_ssim_backward, which writes
+ * grad_pred = grad_scale * d loss[0] / d pred. */
+size_t gs_l1_ssim_workspace_bytes(int height, int width, int channels);
+int gs_l1_ssim_forward(const float* pred, const float* target, int height, int width, int channels,
+                       float lambda_dssim, float max_val, int window_size, float sigma,
+                       void* workspace, size_t workspace_bytes, float* loss, void* stream);
+int gs_l1_ssim_backward(const float* pred, const float* target, int height, int width, int channels,
+                        float lambda_dssim, float max_val, int window_size, float sigma,
+                        const void* workspace, size_t workspace_bytes, float grad_scale,
+                        float* grad_pred, void* stream);
+
+/* Per-parameter Adam (mlx.optimizers.Adam as the trainer builds it,
+ * trainer.py:128, update order of Adam.apply_single): per group
+ *   m = b1 m + (1 - b1) g,  v = b2 v + (1 - b2) g^2,
+ *   p -= lr m / (sqrt(v) + eps)                                  (bias_correction = 0)
+ *   p -= (lr / (1 - b1^step)) m / (sqrt(v) / sqrt(1 - b2^step) + eps)  (bias_correction = 1)
+ * All groups in one launch; `step` is the 1-based update count.  The betas are
+ * doubles: b1, b2 and 1 - b1, 1 - b2 are each rounded to float32 from the
+ * double value, as MLX does with the Python floats it is given. */
+#define GS_ADAM_MAX_GROUPS 8
+typedef struct gs_adam_group {
+  float* param;
+  const float* grad;
+  float* m;
+  float* v;
+  int64_t n;
+  float lr;
+} gs_adam_group;
+int gs_adam_step(const gs_adam_group* groups, int n_groups, double beta1, double beta2, float eps,
+                 int bias_correction, int64_t step, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

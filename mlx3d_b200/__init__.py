@@ -6,7 +6,7 @@ CUDA, see include/gsplat_b200.h); tensors are torch CUDA tensors.
 
 __version__ = "0.1.0"
 
-from . import cameras, renderer, splatting  # noqa: E402
+from . import cameras, losses, renderer, splatting  # noqa: E402
 from .cameras import Camera  # noqa: E402
 
-__all__ = ["Camera", "cameras", "renderer", "splatting", "__version__"]
+__all__ = ["Camera", "cameras", "losses", "renderer", "splatting", "__version__"]

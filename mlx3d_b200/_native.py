@@ -46,6 +46,21 @@ class GsCamera(ctypes.Structure):
     ]
 
 
+class GsAdamGroup(ctypes.Structure):
+    """Mirror of ``gs_adam_group`` in include/gsplat_b200.h."""
+
+    _fields_ = [
+        ("param", c_void_p),
+        ("grad", c_void_p),
+        ("m", c_void_p),
+        ("v", c_void_p),
+        ("n", c_int64),
+        ("lr", c_float),
+    ]
+
+
+GS_ADAM_MAX_GROUPS = 8
+
 # name -> (restype, argtypes)
 _P = c_void_p
 _SIGS = {
@@ -80,6 +95,14 @@ _SIGS = {
     "gs_bin_gaussians_static": (
         c_int, [_P, _P, _P, c_int64, c_int, c_int, c_int64, _P, _P, ctypes.POINTER(c_int64), _P]
     ),
+    "gs_l1_ssim_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "gs_l1_ssim_forward": (
+        c_int, [_P, _P, c_int, c_int, c_int, c_float, c_float, c_int, c_float, _P, c_size_t, _P, _P]
+    ),
+    "gs_l1_ssim_backward": (
+        c_int, [_P, _P, c_int, c_int, c_int, c_float, c_float, c_int, c_float, _P, c_size_t, c_float, _P, _P]
+    ),
+    "gs_adam_step": (c_int, [POINTER(GsAdamGroup), c_int, ctypes.c_double, ctypes.c_double, c_float, c_int, c_int64, _P]),
     "gs_rasterize_forward": (
         c_int,
         [_P, _P, _P, c_int, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, _P, _P, _P, _P, _P],

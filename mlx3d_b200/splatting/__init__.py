@@ -6,10 +6,13 @@ from .rasterize import rasterize, rasterize_depth, rasterize_features
 from .render import render_gaussian_depth, render_gaussian_features, render_gaussians
 from .sh import eval_sh, num_sh_bases, rgb_to_sh, sh_to_rgb
 from .tiles import TILE_SIZE, bin_gaussians
+from .trainer import GaussianTrainer, TrainerConfig
 
 __all__ = [
     "GaussianModel",
+    "GaussianTrainer",
     "TILE_SIZE",
+    "TrainerConfig",
     "bin_gaussians",
     "eval_sh",
     "num_sh_bases",

@@ -35,6 +35,7 @@ class _RenderCfg:
     sh_degree: int  # -1: colours given directly
     sh_mode: str  # "full" (sh_a = (N, K, 3)), "split" (sh_a = dc (N, 1, 3), sh_b = rest), "colors"
     with_depth: bool
+    probe: object = None  # tensor (N, 2) that receives dL/d means2d of the compositor, or None
 
 
 def _sh_layout(cfg: _RenderCfg, sh_a, sh_b):
@@ -121,6 +122,8 @@ class _Render(torch.autograd.Function):
         )
         if g_means2d_out is not None:
             g_m2d += g_means2d_out
+        if cfg.probe is not None:
+            cfg.probe.copy_(g_m2d)
         g_means = torch.empty_like(means)
         g_quats = torch.empty_like(quats)
         g_scales = torch.empty_like(scales)
@@ -170,6 +173,7 @@ def _render_fused(
     flags: int = 0,
     with_depth: bool = False,
     blur: float = 0.3,
+    probe: torch.Tensor | None = None,
 ) -> dict[str, torch.Tensor]:
     means = nat.require_cuda("means", means)
     quats = nat.require_cuda("quats", quats)
@@ -209,7 +213,7 @@ def _render_fused(
     cfg = _RenderCfg(
         cam=camera.to_native(), width=int(camera.width), height=int(camera.height), blur=float(blur),
         antialias=bool(antialias) and blur > 0, flags=int(flags), sh_degree=degree, sh_mode=mode,
-        with_depth=bool(with_depth),
+        with_depth=bool(with_depth), probe=probe,
     )
     image, final_T, n_contrib, means2d, depths, radii, comp, depth, counts = _Render.apply(
         means, quats, scales, opacities, sh_a, sh_b, colors, background, cfg

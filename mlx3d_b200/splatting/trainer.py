@@ -1,0 +1,200 @@
+"""The 3DGS optimisation recipe (src/mlx3d/splatting/trainer.py) on sm_100a.
+
+One step: fused render (preprocess, binning, compositing) -> fused
+L1 + D-SSIM loss -> fused backward -> one multi-tensor Adam launch over the
+six parameter groups.  Learning rates and schedule follow the reference:
+per-group Adam with eps = 1e-15 and no bias correction (mlx.optimizers.Adam's
+default), ``lr_means`` (times the scene extent) decaying exponentially to
+``lr_means_final`` over ``lr_means_max_steps``; update k uses the schedule's
+value at k - 1 and ``learning_rates()`` reports the rate of the last update
+(the behaviour pinned by the reference's test_trainer_position_lr_decays).
+
+Screen-space positional gradient norms are accumulated for densification
+(trainer.py:357-365), the opacity reset and SH-degree schedule run as in the
+reference; adaptive density control itself (clone / split / prune, MCMC
+relocation, 2DGS constraints — host-side control of the Gaussian set) is not
+part of this package: ``densify`` in the returned info is always ``None``.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import _native as nat
+from ..cameras import Camera
+from ..distributed import allreduce_gradients, world
+from ..losses import l1_dssim_loss
+from .model import GaussianModel
+from .render import _render_fused
+
+__all__ = ["TrainerConfig", "GaussianTrainer"]
+
+_GROUPS = ("means", "scales", "quats", "opacities", "sh_dc", "sh_rest")
+
+
+@dataclass
+class TrainerConfig:
+    """Fields and defaults of trainer.py:27-76 (densification fields kept for
+    API compatibility; only the statistics they gate are computed)."""
+
+    method: str = "vanilla"
+    lr_means: float = 1.6e-4
+    lr_means_final: float = 1.6e-6
+    lr_means_max_steps: int = 30_000
+    lr_scales: float = 5e-3
+    lr_quats: float = 1e-3
+    lr_opacities: float = 5e-2
+    lr_sh_dc: float = 2.5e-3
+    lr_sh_rest: float = 2.5e-3 / 20.0
+    lambda_dssim: float = 0.2
+    antialias: bool = False
+    projection: str = "ewa"
+    densify_from: int = 500
+    densify_until: int = 15000
+    densify_every: int = 100
+    densify_grad_threshold: float = 0.0002
+    opacity_reset_every: int = 3000
+    sh_increase_every: int = 1000
+    white_background: bool = False
+    adam_betas: tuple = (0.9, 0.999)
+    adam_eps: float = 1e-15
+    adam_bias_correction: bool = False
+
+
+class GaussianTrainer:
+    """Optimises a :class:`GaussianModel` against posed images (trainer.py:79-421)."""
+
+    def __init__(self, model: GaussianModel, config: TrainerConfig | None = None, scene_extent: float = 1.0):
+        self.model = model
+        self.config = config or TrainerConfig()
+        if self.config.method != "vanilla":
+            raise ValueError("TrainerConfig.method must be 'vanilla' in mlx3d_b200 ('mcmc' / '2dgs' control "
+                             "the Gaussian set and are not provided)")
+        if self.config.projection not in {"ewa", "ut"}:
+            raise ValueError("TrainerConfig.projection must be 'ewa' or 'ut'")
+        if self.config.projection == "ut":
+            raise NotImplementedError("projection='ut' is not implemented in mlx3d_b200; use 'ewa'.")
+        self.scene_extent = scene_extent
+        self.step_count = 0
+        for k in _GROUPS:
+            p = model.params[k]
+            if not p.is_contiguous() or p.dtype != torch.float32 or p.device.type != "cuda":
+                raise ValueError(f"parameter {k} must be a contiguous float32 CUDA tensor")
+            p.requires_grad_(True)
+        self._m = {k: torch.zeros_like(model.params[k]) for k in _GROUPS}
+        self._v = {k: torch.zeros_like(model.params[k]) for k in _GROUPS}
+        self._lr_last = self._schedule(0)
+        self._reset_grad_accum()
+
+    # ----------------------------------------------------------- schedules
+    def _schedule(self, k: int) -> dict[str, float]:
+        c = self.config
+        lr0 = c.lr_means * self.scene_extent
+        lr1 = c.lr_means_final * self.scene_extent
+        if c.lr_means_max_steps > 0 and lr0 > 0 and lr1 > 0:
+            lr_means = lr0 * ((lr1 / lr0) ** (1.0 / c.lr_means_max_steps)) ** k
+        else:
+            lr_means = lr0
+        return {"means": lr_means, "scales": c.lr_scales, "quats": c.lr_quats, "opacities": c.lr_opacities,
+                "sh_dc": c.lr_sh_dc, "sh_rest": c.lr_sh_rest}
+
+    def learning_rates(self) -> dict[str, float]:
+        """Per-parameter rates of the last update (before any update: of the first)."""
+        return dict(self._lr_last)
+
+    def _reset_grad_accum(self) -> None:
+        n = self.model.num_gaussians
+        dev = self.model.params["means"].device
+        self.grad_accum = torch.zeros((n,), dtype=torch.float32, device=dev)
+        self.grad_count = torch.zeros((n,), dtype=torch.float32, device=dev)
+
+    # ------------------------------------------------------------- pieces
+    def _view_loss(self, camera: Camera, target: torch.Tensor, probe: torch.Tensor | None, scale: float):
+        cfg = self.config
+        dev = self.model.params["means"].device
+        bg = torch.ones(3, device=dev) if cfg.white_background else torch.zeros(3, device=dev)
+        p = self.model.params
+        out = _render_fused(
+            camera, p["means"], p["quats"], p["scales"], p["opacities"], sh_dc=p["sh_dc"], sh_rest=p["sh_rest"],
+            sh_degree=self.model.active_sh_degree, background=bg, antialias=cfg.antialias,
+            flags=nat.GS_ACT_EXP_SCALES | nat.GS_ACT_SIGMOID_OPACITY, probe=probe)
+        loss, _, _ = l1_dssim_loss(out["image"], target, cfg.lambda_dssim)
+        (loss * scale).backward()
+        return loss.detach(), out
+
+    def _adam(self) -> None:
+        self.step_count += 1
+        lrs = self._schedule(self.step_count - 1)
+        self._lr_last = lrs
+        c = self.config
+        groups = (nat.GsAdamGroup * len(_GROUPS))()
+        for i, k in enumerate(_GROUPS):
+            p = self.model.params[k]
+            if p.grad is None:
+                p.grad = torch.zeros_like(p)
+            g = p.grad.contiguous()
+            p.grad = g
+            groups[i] = nat.GsAdamGroup(p.data_ptr(), g.data_ptr(), self._m[k].data_ptr(), self._v[k].data_ptr(),
+                                        p.numel(), lrs[k])
+        nat.call("gs_adam_step", groups, len(_GROUPS), c.adam_betas[0], c.adam_betas[1], c.adam_eps,
+                 int(c.adam_bias_correction), self.step_count, nat.stream())
+        for k in _GROUPS:
+            self.model.params[k].grad = None
+
+    def _schedules_after_update(self) -> tuple[bool, bool]:
+        cfg = self.config
+        opacity_reset = sh_changed = False
+        if self.step_count % cfg.opacity_reset_every == 0 and self.step_count <= cfg.densify_until:
+            with torch.no_grad():
+                logit = math.log(0.01 / 0.99)
+                self.model.params["opacities"].clamp_(max=logit)
+            opacity_reset = True
+        if self.step_count % cfg.sh_increase_every == 0:
+            self.model.one_up_sh_degree()
+            sh_changed = True
+        return opacity_reset, sh_changed
+
+    def _info(self, loss: float, opacity_reset: bool, sh_changed: bool) -> dict:
+        return {"loss": loss, "num_gaussians": self.model.num_gaussians, "step": self.step_count,
+                "active_sh_degree": self.model.active_sh_degree, "lr_means": self.learning_rates()["means"],
+                "method": self.config.method, "densify": None, "opacity_reset": opacity_reset,
+                "sh_degree_changed": sh_changed, "geometry": {}}
+
+    # --------------------------------------------------------------- steps
+    def step(self, camera: Camera, target: torch.Tensor) -> dict:
+        """One optimisation step on a single view (trainer.py:319-421)."""
+        cfg = self.config
+        track = cfg.densify_from <= self.step_count + 1 <= cfg.densify_until
+        probe = torch.zeros((self.model.num_gaussians, 2), device=target.device) if track else None
+        loss, out = self._view_loss(camera, target, probe, 1.0)
+        self._adam()
+        if track:
+            with torch.no_grad():
+                g = probe * torch.tensor([camera.width / 2.0, camera.height / 2.0], device=probe.device)
+                visible = (out["radii"] > 0).float()
+                self.grad_accum += g.norm(dim=-1) * visible
+                self.grad_count += visible
+        opacity_reset, sh_changed = self._schedules_after_update()
+        return self._info(float(loss), opacity_reset, sh_changed)
+
+    def step_views(self, cameras: list[Camera], targets: list[torch.Tensor], total_views: int | None = None) -> dict:
+        """One data-parallel step over a batch of views: this rank renders
+        ``cameras`` (its shard), the loss is averaged over ``total_views``
+        (all ranks' views), gradients are summed over ranks (NCCL all-reduce)
+        and one Adam update is applied on every rank."""
+        rank, ws = world()
+        if total_views is None:
+            total_views = len(cameras) * ws
+        loss_sum = torch.zeros((), device=self.model.params["means"].device)
+        for cam, tgt in zip(cameras, targets):
+            loss, _ = self._view_loss(cam, tgt, None, 1.0 / total_views)
+            loss_sum += loss
+        allreduce_gradients({k: self.model.params[k] for k in _GROUPS})
+        self._adam()
+        opacity_reset, sh_changed = self._schedules_after_update()
+        info = self._info(float(loss_sum) / max(len(cameras), 1), opacity_reset, sh_changed)
+        info["views"] = len(cameras)
+        return info

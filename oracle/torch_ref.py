@@ -9,6 +9,10 @@ differentiation (the reference gets these gradients from MLX autodiff):
 * ``view_dirs``   — src/mlx3d/splatting/render.py:77-78
 * ``naive_render``— src/mlx3d/splatting/reference.py:16-74, the reference's own
   O(N*H*W) test oracle (small scenes only).
+* ``ssim`` / ``l1_dssim``   — src/mlx3d/losses/image_metrics.py:23-85 and the
+  trainer's loss, trainer.py:300-305 (depthwise conv2d, zero padding).
+* ``adam_update`` — mlx.optimizers.Adam.apply_single as the trainer builds it
+  (trainer.py:128), float32 numpy, one rounding per operation.
 
 The product package never imports this module.
 """
@@ -154,3 +158,39 @@ def naive_render(camera, means, quats, scales, opacities, colors, background=Non
     final_T = torch.prod(torch.where(keep, one_minus, torch.ones_like(one_minus)), dim=0)
     image = image + final_T[..., None] * background
     return {"image": image, "alpha": 1.0 - final_T, "final_T": final_T}
+
+
+def ssim(pred, target, max_val=1.0, window_size=11, sigma=1.5):
+    """image_metrics.py:29-85 for (H, W, C) images."""
+    dt = pred.dtype
+    x = torch.arange(window_size, dtype=torch.float32) - (window_size - 1) / 2.0
+    g = torch.exp(-(x * x) / (2.0 * sigma * sigma))
+    g = (g / g.sum()).to(dt)
+    win = g[:, None] * g[None, :]
+    C = pred.shape[-1]
+    w = win[None, None].expand(C, 1, window_size, window_size)
+    p = pred.permute(2, 0, 1)[None]
+    t = target.permute(2, 0, 1)[None]
+    filt = lambda a: torch.nn.functional.conv2d(a, w, padding=window_size // 2, groups=C)  # noqa: E731
+    mu_p, mu_t = filt(p), filt(t)
+    sp = filt(p * p) - mu_p * mu_p
+    st = filt(t * t) - mu_t * mu_t
+    spt = filt(p * t) - mu_p * mu_t
+    c1, c2 = (0.01 * max_val) ** 2, (0.03 * max_val) ** 2
+    cs = (2.0 * spt + c2) / (sp + st + c2)
+    return ((2.0 * mu_p * mu_t + c1) / (mu_p * mu_p + mu_t * mu_t + c1) * cs).mean()
+
+
+def l1_dssim(pred, target, lam=0.2):
+    return (1.0 - lam) * (pred - target).abs().mean() + lam * (1.0 - ssim(pred, target))
+
+
+def adam_update(p, g, m, v, lr, b1=0.9, b2=0.999, eps=1e-15):
+    """One update in float32 numpy (arrays updated and returned)."""
+    import numpy as np
+
+    f = np.float32
+    m = f(b1) * m + f(1.0 - b1) * g
+    v = f(b2) * v + f(1.0 - b2) * (g * g)
+    p = p - (f(lr) * m) / (np.sqrt(v) + f(eps))
+    return p.astype(np.float32), m.astype(np.float32), v.astype(np.float32)
