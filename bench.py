@@ -42,6 +42,7 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--config", type=int, default=2, help="scene config (2 = the headline workload)")
     ap.add_argument("--n", type=int, default=None, help="override the Gaussian count (profiling runs)")
+    ap.add_argument("--views", type=int, default=None, help="override the view count (configs 3 and 4)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     return ap.parse_args()
@@ -427,11 +428,106 @@ def run_reference(args, world, rank):
     }
 
 
+# ------------------------------------------------- multi-view configurations
+def run_multiview(args, world, rank, local):
+    """C3 (data-parallel training step: every rank renders its shard of the 64
+    views, L1 + D-SSIM, gradient all-reduce, one Adam update) or C4 (render
+    only, with depth: every rank renders its shard of the 256 views).  Strong
+    scaling: the view batch is fixed, ranks split it.  Metric: views/s."""
+    import torch
+    import torch.distributed as dist
+
+    from mlx3d_b200 import _native as nat
+    from mlx3d_b200.distributed import shard_views
+    from mlx3d_b200.scenes import make_scene
+    from mlx3d_b200.splatting import GaussianModel, GaussianTrainer, TrainerConfig
+
+    dev = torch.device("cuda", local)
+    scene = make_scene(args.config, n=args.n, views=args.views)
+    cfg = scene.config
+    idx = shard_views(list(range(len(scene.cameras))), rank, world)
+    cams = [scene.cameras[i] for i in idx]
+    params = scene.torch_params(device=dev)
+    model = GaussianModel(params, sh_degree=3)
+    model.active_sh_degree = cfg.sh_degree
+    dups = []
+    if cfg.index == 3:
+        targets = [scene.target(i, device=dev) for i in idx]
+        trainer = GaussianTrainer(model, TrainerConfig(antialias=cfg.antialias, densify_from=10**9,
+                                                       opacity_reset_every=10**9, sh_increase_every=10**9))
+
+        def step():
+            trainer.step_views(cams, targets, total_views=len(scene.cameras))
+    else:
+        def step():
+            with torch.no_grad():
+                for cam in cams:
+                    out = model.render(cam, antialias=cfg.antialias, render_depth=True)
+                    dups.append(out["n_duplicates"])
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    barrier()
+    dups.clear()
+    lib = nat.load()
+    l0 = lib.gs_kernel_launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clocks:
+        e0.record()
+        for _ in range(args.steps):
+            step()
+        e1.record()
+        torch.cuda.synchronize()
+    barrier()
+    launches = lib.gs_kernel_launch_count() - l0
+    t = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
+    keys = torch.tensor([float(sum(dups)) / max(args.steps, 1)], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(keys)
+    ms = float(t.item())
+    views = len(scene.cameras)
+    if rank != 0:
+        return None
+    n = scene.params["means"].shape[0]
+    what = "training step (L1 + D-SSIM, all-reduce, Adam)" if cfg.index == 3 else "render + depth, forward only"
+    line = {
+        "metric": f"C{cfg.index} views/s ({what})",
+        "value": round(1000.0 * views / ms, 2),
+        "unit": "views/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 3),
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded PCG64 scene of BASELINE config %d)" % cfg.index,
+        "config": {"workload": f"C{cfg.index}: {n:,} Gaussians, SH{cfg.sh_degree}, {views} views "
+                               f"{cfg.width}x{cfg.height}, fov {cfg.fov:g}, antialias={cfg.antialias}; {what}",
+                   "views_per_step": views, "parallelism": f"views sharded over {world} GPU(s)",
+                   "l2": "no flush: per-step working set exceeds the 126 MB L2"},
+        "gpu_launches": int(launches),
+        "clocks": clocks.summary(),
+    }
+    if cfg.index == 4:
+        line["sort_keys_per_s"] = round(float(keys.item()) / (ms * 1e-3), 1)
+    return line
+
+
 def main():
     args = parse_args()
     world, rank, local = dist_setup(args)
     if args.impl == "reference":
         line = run_reference(args, world, rank)
+    elif args.config in (3, 4):
+        line = run_multiview(args, world, rank, local)
     else:
         line = run_ours(args, world, rank, local)
     if line is not None:

@@ -36,6 +36,7 @@ class _RenderCfg:
     sh_mode: str  # "full" (sh_a = (N, K, 3)), "split" (sh_a = dc (N, 1, 3), sh_b = rest), "colors"
     with_depth: bool
     probe: object = None  # tensor (N, 2) that receives dL/d means2d of the compositor, or None
+    duplicates: int = 0  # set by the forward: (Gaussian, tile) pairs D of this frame
 
 
 def _sh_layout(cfg: _RenderCfg, sh_a, sh_b):
@@ -76,6 +77,7 @@ class _Render(torch.autograd.Function):
             nat.ptr(opac_out), nat.ptr(counts), s,
         )
         sorted_ids, tile_ranges = bin_with_counts(means2d, radii, depths, counts, W, H)
+        cfg.duplicates = int(sorted_ids.shape[0])
         image = torch.empty((H, W, 3), **f32)
         final_T = torch.empty((H, W), **f32)
         n_contrib = torch.empty((H, W), device=dev, dtype=torch.int32)
@@ -230,6 +232,7 @@ def _render_fused(
     }
     if depth is not None:
         out["depth"] = depth
+    out["n_duplicates"] = cfg.duplicates
     return out
 
 
