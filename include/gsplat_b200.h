@@ -158,6 +158,18 @@ int gs_bin_end(const float* means2d, const float* radii, int64_t n, int64_t d, i
                int height, void* ws_n, size_t ws_n_bytes, void* ws_d, size_t ws_d_bytes,
                int32_t* sorted_ids, int32_t* tile_ranges, void* stream);
 
+/* bin_gaussians with the reference's refine_tiles option (`conics` given,
+ * tiles.py:91-164): a (Gaussian, tile) duplicate of the square bounding box
+ * is kept only if the minimum of the conic form a dx^2 + 2 b dx dy + c dy^2
+ * over the tile rectangle is <= 12.  gs_tile_counts_refined replaces
+ * gs_tile_counts (kept tiles per Gaussian), gs_bin_end_refined replaces
+ * gs_bin_end; gs_bin_begin is shared.  conics (N,3) as gs_project_forward. */
+int gs_tile_counts_refined(const float* means2d, const float* radii, const float* conics, int64_t n,
+                           int width, int height, int32_t* tiles_touched, void* stream);
+int gs_bin_end_refined(const float* means2d, const float* radii, const float* conics, int64_t n,
+                       int64_t d, int width, int height, void* ws_n, size_t ws_n_bytes, void* ws_d,
+                       size_t ws_d_bytes, int32_t* sorted_ids, int32_t* tile_ranges, void* stream);
+
 /* No-allocation binning.  Has no counterpart in the reference: it exists
  * for callers that cannot allocate device memory (a renderer embedded in an
  * application whose GPU memory belongs to another allocator, a plugin host,

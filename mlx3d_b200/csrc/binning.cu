@@ -269,29 +269,89 @@ k_scan_down(const int32_t* __restrict__ counts, const int32_t* __restrict__ perm
   }
 }
 
-// One thread per Gaussian in depth order: write (tile id, Gaussian id) for
-// every tile of its rectangle, row-major (tiles.py:77-89).
-__global__ void k_duplicate(const float* __restrict__ means2d, const float* __restrict__ radii,
-                            const int32_t* __restrict__ perm, const uint32_t* __restrict__ offsets,
-                            int64_t n, int64_t d, int width, int height, int tiles_x,
-                            int tiles_y, uint32_t* __restrict__ tkeys, int32_t* __restrict__ tvals) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  const int32_t g = perm[i];
-  const float2 m = reinterpret_cast<const float2*>(means2d)[g];
-  const float r = radii[g];
+// AccuTile refinement of one (Gaussian, tile) pair (tiles.py:91-141): the
+// exact minimum over the tile rectangle of the conic form
+// a dx^2 + 2 b dx dy + c dy^2 (corners plus the four clipped edge
+// minimisers; 0 when the centre lies inside), kept if <= 12.  Float32
+// operations in the reference's order.
+__device__ __forceinline__ bool refine_keep(const float* __restrict__ co, float gx, float gy, int tx,
+                                            int ty, int width, int height) {
+  const float x0 = (float)(tx * GS_TILE), y0 = (float)(ty * GS_TILE);
+  const float x1 = (float)min((tx + 1) * GS_TILE, width), y1 = (float)min((ty + 1) * GS_TILE, height);
+  const float dxl = gs_sub(x0, gx), dxr = gs_sub(x1, gx);
+  const float dyb = gs_sub(y0, gy), dyt = gs_sub(y1, gy);
+  const float a = co[0], b = co[1], c = co[2];
+  const float b2 = gs_mul(2.0f, b);
+  auto q = [&](float dx, float dy) {
+    return gs_add(gs_add(gs_mul(gs_mul(a, dx), dx), gs_mul(gs_mul(b2, dx), dy)), gs_mul(gs_mul(c, dy), dy));
+  };
+  auto clip = [](float v, float lo, float hi) { return gs_minf(gs_maxf(v, lo), hi); };
+  const float nbc = -gs_div(b, c), nba = -gs_div(b, a);
+  const float dy_left = clip(gs_mul(nbc, dxl), dyb, dyt);
+  const float dy_right = clip(gs_mul(nbc, dxr), dyb, dyt);
+  const float dx_bottom = clip(gs_mul(nba, dyb), dxl, dxr);
+  const float dx_top = clip(gs_mul(nba, dyt), dxl, dxr);
+  float qm = q(dxl, dyb);
+  qm = gs_minf(qm, q(dxl, dyt));
+  qm = gs_minf(qm, q(dxr, dyb));
+  qm = gs_minf(qm, q(dxr, dyt));
+  qm = gs_minf(qm, q(dxl, dy_left));
+  qm = gs_minf(qm, q(dxr, dy_right));
+  qm = gs_minf(qm, q(dx_bottom, dyb));
+  qm = gs_minf(qm, q(dx_top, dyt));
+  const bool inside = dxl <= 0.0f && dxr >= 0.0f && dyb <= 0.0f && dyt >= 0.0f;
+  return (inside ? 0.0f : qm) <= 12.0f;
+}
+
+// Inclusive tile rectangle of an on-screen Gaussian (tiles.py:54-62); false
+// when it touches no tile.
+__device__ __forceinline__ bool gauss_rect(float2 m, float r, int width, int height, int tiles_x,
+                                           int tiles_y, int& x0, int& y0, int& x1, int& y1) {
   const float fx1 = (float)(tiles_x - 1), fy1 = (float)(tiles_y - 1);
   const float T = (float)GS_TILE;
   const bool on = (r > 0.0f) && (gs_add(m.x, r) >= 0.0f) && (gs_sub(m.x, r) < (float)width) &&
                   (gs_add(m.y, r) >= 0.0f) && (gs_sub(m.y, r) < (float)height);
-  if (!on) return;
-  const int x0 = (int)gs_minf(gs_maxf(floorf(gs_div(gs_sub(m.x, r), T)), 0.0f), fx1);
-  const int x1 = (int)gs_minf(gs_maxf(floorf(gs_div(gs_add(m.x, r), T)), 0.0f), fx1);
-  const int y0 = (int)gs_minf(gs_maxf(floorf(gs_div(gs_sub(m.y, r), T)), 0.0f), fy1);
-  const int y1 = (int)gs_minf(gs_maxf(floorf(gs_div(gs_add(m.y, r), T)), 0.0f), fy1);
+  if (!on) return false;
+  x0 = (int)gs_minf(gs_maxf(floorf(gs_div(gs_sub(m.x, r), T)), 0.0f), fx1);
+  x1 = (int)gs_minf(gs_maxf(floorf(gs_div(gs_add(m.x, r), T)), 0.0f), fx1);
+  y0 = (int)gs_minf(gs_maxf(floorf(gs_div(gs_sub(m.y, r), T)), 0.0f), fy1);
+  y1 = (int)gs_minf(gs_maxf(floorf(gs_div(gs_add(m.y, r), T)), 0.0f), fy1);
+  return true;
+}
+
+// Tiles kept by the refinement, per Gaussian (the refined "tiles touched").
+__global__ void k_tile_counts_refined(const float* __restrict__ means2d, const float* __restrict__ radii,
+                                      const float* __restrict__ conics, int64_t n, int width, int height,
+                                      int tiles_x, int tiles_y, int32_t* __restrict__ counts) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const float2 m = reinterpret_cast<const float2*>(means2d)[i];
+  int x0, y0, x1, y1, c = 0;
+  if (gauss_rect(m, radii[i], width, height, tiles_x, tiles_y, x0, y0, x1, y1))
+    for (int ty = y0; ty <= y1; ++ty)
+      for (int tx = x0; tx <= x1; ++tx) c += refine_keep(conics + 3 * i, m.x, m.y, tx, ty, width, height);
+  counts[i] = c;
+}
+
+// One thread per Gaussian in depth order: write (tile id, Gaussian id) for
+// every tile of its rectangle, row-major (tiles.py:77-89), or, with REFINE,
+// for every tile the refinement keeps (tiles.py:141-163).
+template <bool REFINE>
+__global__ void k_duplicate(const float* __restrict__ means2d, const float* __restrict__ radii,
+                            const float* __restrict__ conics, const int32_t* __restrict__ perm,
+                            const uint32_t* __restrict__ offsets, int64_t n, int64_t d, int width,
+                            int height, int tiles_x, int tiles_y, uint32_t* __restrict__ tkeys,
+                            int32_t* __restrict__ tvals) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const int32_t g = perm[i];
+  const float2 m = reinterpret_cast<const float2*>(means2d)[g];
+  int x0, y0, x1, y1;
+  if (!gauss_rect(m, radii[g], width, height, tiles_x, tiles_y, x0, y0, x1, y1)) return;
   uint32_t o = offsets[i];
   for (int ty = y0; ty <= y1; ++ty)
     for (int tx = x0; tx <= x1; ++tx) {
+      if (REFINE && !refine_keep(conics + 3 * (int64_t)g, m.x, m.y, tx, ty, width, height)) continue;
       if ((int64_t)o >= d) return;  // never past the caller's D (counts are recomputed exactly)
       tkeys[o] = (uint32_t)(ty * tiles_x + tx);
       tvals[o] = g;
@@ -395,6 +455,52 @@ static int tile_bits(int num_tiles) {
 
 using namespace gs;
 
+static int bin_end_impl(const float* means2d, const float* radii, const float* conics, int64_t n, int64_t d, int width,
+               int height, void* ws_n, size_t ws_n_bytes, void* ws_d, size_t ws_d_bytes,
+               int32_t* sorted_ids, int32_t* tile_ranges, void* stream) {
+  clear_error();
+  cudaStream_t s = as_stream(stream);
+  if (width <= 0 || height <= 0) return set_error(GS_ERR_INVALID_ARG, "image size must be positive");
+  if (d < 0 || d > INT32_MAX)
+    return set_error(GS_ERR_CAPACITY, "duplicate count %lld exceeds int32 range", (long long)d);
+  const int tiles_x = (int)ceil_div(width, GS_TILE), tiles_y = (int)ceil_div(height, GS_TILE);
+  const int num_tiles = tiles_x * tiles_y;
+  if (!tile_ranges) return set_error(GS_ERR_INVALID_ARG, "tile_ranges is NULL");
+  if (cudaMemsetAsync(tile_ranges, 0, sizeof(int32_t) * 2 * (size_t)num_tiles, s) != cudaSuccess)
+    return set_error(GS_ERR_CUDA, "cudaMemsetAsync failed");
+  if (d == 0 || n == 0) return GS_OK;
+  const NLayout L(n);
+  const DLayout M(d);
+  if (!ws_n || ws_n_bytes < L.total)
+    return set_error(GS_ERR_CAPACITY, "workspace_n too small: %zu < %zu", ws_n_bytes, L.total);
+  if (!ws_d || ws_d_bytes < M.total)
+    return set_error(GS_ERR_CAPACITY, "workspace_d too small: %zu < %zu", ws_d_bytes, M.total);
+  if (!means2d || !radii || !sorted_ids) return set_error(GS_ERR_INVALID_ARG, "gs_bin_end: NULL pointer");
+  const int32_t* perm = at<int32_t>(ws_n, L.vals0);
+  const uint32_t* offsets = at<uint32_t>(ws_n, L.offsets);
+  uint32_t* tk0 = at<uint32_t>(ws_d, M.keys0);
+  uint32_t* tk1 = at<uint32_t>(ws_d, M.keys1);
+  int32_t* tv0 = at<int32_t>(ws_d, M.vals0);
+  int32_t* tv1 = at<int32_t>(ws_d, M.vals1);
+  if (conics)
+    k_duplicate<true><<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(
+        means2d, radii, conics, perm, offsets, n, d, width, height, tiles_x, tiles_y, tk0, tv0);
+  else
+    k_duplicate<false><<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(
+        means2d, radii, nullptr, perm, offsets, n, d, width, height, tiles_x, tiles_y, tk0, tv0);
+  if (int e = check_launch("k_duplicate")) return e;
+  const int bits = tile_bits(num_tiles);
+  const int passes = bits == 0 ? 1 : (bits + 7) / 8;
+  // Final keys land in whichever key buffer the last pass does not read.
+  uint32_t* kfinal = (passes % 2 == 1) ? tk1 : tk0;
+  int e = radix_sort(tk0, tv0, tk1, tv1, d, passes, at<uint32_t>(ws_d, M.hist),
+                     at<uint32_t>(ws_d, M.gtot), M.nb_rs, kfinal, sorted_ids, s);
+  if (e) return e;
+  k_tile_ranges<<<(unsigned)ceil_div(d, 256), 256, 0, s>>>(kfinal, d, tile_ranges);
+  return check_launch("k_tile_ranges");
+}
+
+
 extern "C" {
 
 size_t gs_bin_workspace_n_bytes(int64_t n) { return NLayout(n < 0 ? 0 : n).total; }
@@ -438,42 +544,30 @@ int gs_bin_begin(const float* depths, const int32_t* tiles_touched, int64_t n, v
 int gs_bin_end(const float* means2d, const float* radii, int64_t n, int64_t d, int width,
                int height, void* ws_n, size_t ws_n_bytes, void* ws_d, size_t ws_d_bytes,
                int32_t* sorted_ids, int32_t* tile_ranges, void* stream) {
+  return bin_end_impl(means2d, radii, nullptr, n, d, width, height, ws_n, ws_n_bytes, ws_d, ws_d_bytes,
+                      sorted_ids, tile_ranges, stream);
+}
+
+int gs_bin_end_refined(const float* means2d, const float* radii, const float* conics, int64_t n,
+                       int64_t d, int width, int height, void* ws_n, size_t ws_n_bytes, void* ws_d,
+                       size_t ws_d_bytes, int32_t* sorted_ids, int32_t* tile_ranges, void* stream) {
+  if (!conics && n > 0) return set_error(GS_ERR_INVALID_ARG, "gs_bin_end_refined: conics is NULL");
+  return bin_end_impl(means2d, radii, conics, n, d, width, height, ws_n, ws_n_bytes, ws_d, ws_d_bytes,
+                      sorted_ids, tile_ranges, stream);
+}
+
+int gs_tile_counts_refined(const float* means2d, const float* radii, const float* conics, int64_t n,
+                           int width, int height, int32_t* tiles_touched, void* stream) {
   clear_error();
-  cudaStream_t s = as_stream(stream);
   if (width <= 0 || height <= 0) return set_error(GS_ERR_INVALID_ARG, "image size must be positive");
-  if (d < 0 || d > INT32_MAX)
-    return set_error(GS_ERR_CAPACITY, "duplicate count %lld exceeds int32 range", (long long)d);
-  const int tiles_x = (int)ceil_div(width, GS_TILE), tiles_y = (int)ceil_div(height, GS_TILE);
-  const int num_tiles = tiles_x * tiles_y;
-  if (!tile_ranges) return set_error(GS_ERR_INVALID_ARG, "tile_ranges is NULL");
-  if (cudaMemsetAsync(tile_ranges, 0, sizeof(int32_t) * 2 * (size_t)num_tiles, s) != cudaSuccess)
-    return set_error(GS_ERR_CUDA, "cudaMemsetAsync failed");
-  if (d == 0 || n == 0) return GS_OK;
-  const NLayout L(n);
-  const DLayout M(d);
-  if (!ws_n || ws_n_bytes < L.total)
-    return set_error(GS_ERR_CAPACITY, "workspace_n too small: %zu < %zu", ws_n_bytes, L.total);
-  if (!ws_d || ws_d_bytes < M.total)
-    return set_error(GS_ERR_CAPACITY, "workspace_d too small: %zu < %zu", ws_d_bytes, M.total);
-  if (!means2d || !radii || !sorted_ids) return set_error(GS_ERR_INVALID_ARG, "gs_bin_end: NULL pointer");
-  const int32_t* perm = at<int32_t>(ws_n, L.vals0);
-  const uint32_t* offsets = at<uint32_t>(ws_n, L.offsets);
-  uint32_t* tk0 = at<uint32_t>(ws_d, M.keys0);
-  uint32_t* tk1 = at<uint32_t>(ws_d, M.keys1);
-  int32_t* tv0 = at<int32_t>(ws_d, M.vals0);
-  int32_t* tv1 = at<int32_t>(ws_d, M.vals1);
-  k_duplicate<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(means2d, radii, perm, offsets, n, d, width,
-                                                         height, tiles_x, tiles_y, tk0, tv0);
-  if (int e = check_launch("k_duplicate")) return e;
-  const int bits = tile_bits(num_tiles);
-  const int passes = bits == 0 ? 1 : (bits + 7) / 8;
-  // Final keys land in whichever key buffer the last pass does not read.
-  uint32_t* kfinal = (passes % 2 == 1) ? tk1 : tk0;
-  int e = radix_sort(tk0, tv0, tk1, tv1, d, passes, at<uint32_t>(ws_d, M.hist),
-                     at<uint32_t>(ws_d, M.gtot), M.nb_rs, kfinal, sorted_ids, s);
-  if (e) return e;
-  k_tile_ranges<<<(unsigned)ceil_div(d, 256), 256, 0, s>>>(kfinal, d, tile_ranges);
-  return check_launch("k_tile_ranges");
+  if (n <= 0) return GS_OK;
+  if (!means2d || !radii || !conics || !tiles_touched)
+    return set_error(GS_ERR_INVALID_ARG, "gs_tile_counts_refined: NULL pointer");
+  if (!aligned(means2d, 8)) return set_error(GS_ERR_INVALID_ARG, "means2d must be 8-byte aligned");
+  const int tx = (int)ceil_div(width, GS_TILE), ty = (int)ceil_div(height, GS_TILE);
+  k_tile_counts_refined<<<(unsigned)ceil_div(n, 256), 256, 0, as_stream(stream)>>>(
+      means2d, radii, conics, n, width, height, tx, ty, tiles_touched);
+  return check_launch("k_tile_counts_refined");
 }
 
 }  // extern "C"

@@ -36,6 +36,7 @@ class _RenderCfg:
     sh_mode: str  # "full" (sh_a = (N, K, 3)), "split" (sh_a = dc (N, 1, 3), sh_b = rest), "colors"
     with_depth: bool
     probe: object = None  # tensor (N, 2) that receives dL/d means2d of the compositor, or None
+    refine: bool = False  # AccuTile refinement of the tile duplicates (tiles.py:91-164)
     duplicates: int = 0  # set by the forward: (Gaussian, tile) pairs D of this frame
 
 
@@ -76,7 +77,11 @@ class _Render(torch.autograd.Function):
             nat.ptr(conics), nat.ptr(depths), nat.ptr(radii), nat.ptr(comp), nat.ptr(col) if use_sh else None,
             nat.ptr(opac_out), nat.ptr(counts), s,
         )
-        sorted_ids, tile_ranges = bin_with_counts(means2d, radii, depths, counts, W, H)
+        if cfg.refine:
+            nat.call("gs_tile_counts_refined", nat.ptr(means2d), nat.ptr(radii), nat.ptr(conics), n, W, H,
+                     nat.ptr(counts), s)
+        sorted_ids, tile_ranges = bin_with_counts(means2d, radii, depths, counts, W, H,
+                                                  conics if cfg.refine else None)
         cfg.duplicates = int(sorted_ids.shape[0])
         image = torch.empty((H, W, 3), **f32)
         final_T = torch.empty((H, W), **f32)
@@ -176,6 +181,7 @@ def _render_fused(
     with_depth: bool = False,
     blur: float = 0.3,
     probe: torch.Tensor | None = None,
+    refine_tiles: bool = False,
 ) -> dict[str, torch.Tensor]:
     means = nat.require_cuda("means", means)
     quats = nat.require_cuda("quats", quats)
@@ -215,7 +221,7 @@ def _render_fused(
     cfg = _RenderCfg(
         cam=camera.to_native(), width=int(camera.width), height=int(camera.height), blur=float(blur),
         antialias=bool(antialias) and blur > 0, flags=int(flags), sh_degree=degree, sh_mode=mode,
-        with_depth=bool(with_depth), probe=probe,
+        with_depth=bool(with_depth), probe=probe, refine=bool(refine_tiles),
     )
     image, final_T, n_contrib, means2d, depths, radii, comp, depth, counts = _Render.apply(
         means, quats, scales, opacities, sh_a, sh_b, colors, background, cfg
@@ -270,22 +276,19 @@ def render_gaussians(
     if (colors is None) == (sh is None):
         raise ValueError("Provide exactly one of `colors` or `sh`.")
     _check_projection(projection)
-    if refine_tiles:
-        raise NotImplementedError("refine_tiles (AccuTile culling) is not implemented in mlx3d_b200.")
     return _render_fused(
         camera, means, quats, scales, opacities, colors=colors, sh=sh, sh_degree=sh_degree, background=background,
-        antialias=antialias, with_depth=render_depth,
+        antialias=antialias, with_depth=render_depth, refine_tiles=refine_tiles,
     )
 
 
 def _project_and_bin(camera, means, quats, scales, opacities, refine_tiles, antialias, projection):
     _check_projection(projection)
-    if refine_tiles:
-        raise NotImplementedError("refine_tiles (AccuTile culling) is not implemented in mlx3d_b200.")
     proj = project_gaussians(camera, means, quats, scales, antialias=antialias)
     opac = nat.require_cuda("opacities", opacities).reshape(-1) * proj["compensation"]
     sorted_ids, tile_ranges, tiles_x, tiles_y = bin_gaussians(
-        proj["means2d"], proj["radii"], proj["depths"], camera.width, camera.height
+        proj["means2d"], proj["radii"], proj["depths"], camera.width, camera.height,
+        conics=proj["conics"] if refine_tiles else None,
     )
     return proj, opac, sorted_ids, tile_ranges, tiles_x, tiles_y
 

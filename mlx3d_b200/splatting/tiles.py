@@ -24,9 +24,11 @@ def bin_with_counts(
     tiles_touched: torch.Tensor,
     width: int,
     height: int,
+    conics: torch.Tensor | None = None,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Depth order, duplicates, tile sort and ranges, given per-Gaussian tile
-    counts already computed (by the fused preprocess kernel or gs_tile_counts)."""
+    counts already computed (by the fused preprocess kernel, gs_tile_counts, or
+    gs_tile_counts_refined when ``conics`` is given for the tile refinement)."""
     n = means2d.shape[0]
     dev = means2d.device
     tiles_x = (width + TILE_SIZE - 1) // TILE_SIZE
@@ -41,10 +43,17 @@ def bin_with_counts(
     ws_d = torch.empty((max(1, lib.gs_bin_workspace_d_bytes(d)),), device=dev, dtype=torch.uint8)
     sorted_ids = torch.empty((d,), device=dev, dtype=torch.int32)
     tile_ranges = torch.empty((tiles_x * tiles_y, 2), device=dev, dtype=torch.int32)
-    nat.call(
-        "gs_bin_end", nat.ptr(means2d), nat.ptr(radii), n, d, width, height, nat.ptr(ws_n), ws_n.numel(),
-        nat.ptr(ws_d), ws_d.numel(), nat.ptr(sorted_ids) if d else None, nat.ptr(tile_ranges), s,
-    )
+    if conics is None:
+        nat.call(
+            "gs_bin_end", nat.ptr(means2d), nat.ptr(radii), n, d, width, height, nat.ptr(ws_n), ws_n.numel(),
+            nat.ptr(ws_d), ws_d.numel(), nat.ptr(sorted_ids) if d else None, nat.ptr(tile_ranges), s,
+        )
+    else:
+        nat.call(
+            "gs_bin_end_refined", nat.ptr(means2d), nat.ptr(radii), nat.ptr(conics), n, d, width, height,
+            nat.ptr(ws_n), ws_n.numel(), nat.ptr(ws_d), ws_d.numel(), nat.ptr(sorted_ids) if d else None,
+            nat.ptr(tile_ranges), s,
+        )
     return sorted_ids, tile_ranges
 
 
@@ -58,11 +67,11 @@ def bin_gaussians(
 ) -> tuple[torch.Tensor, torch.Tensor, int, int]:
     """Assign Gaussians to 16x16 tiles and sort by (tile, depth) (tiles.py:19-182).
 
-    Returns ``(sorted_ids, tile_ranges, tiles_x, tiles_y)``.  No gradients
-    flow through binning (the reference stop-gradients its inputs).
+    Returns ``(sorted_ids, tile_ranges, tiles_x, tiles_y)``.  With ``conics``
+    (N, 3), duplicates whose tile rectangle cannot reach the Gaussian's
+    conic distance 12 are dropped (tiles.py:91-164).  No gradients flow
+    through binning (the reference stop-gradients its inputs).
     """
-    if conics is not None:
-        raise NotImplementedError("refine_tiles (AccuTile culling) is not implemented in mlx3d_b200.")
     means2d = nat.require_cuda("means2d", means2d.detach())
     radii = nat.require_cuda("radii", radii.detach())
     depths = nat.require_cuda("depths", depths.detach())
@@ -72,6 +81,14 @@ def bin_gaussians(
     tiles_x = (width + TILE_SIZE - 1) // TILE_SIZE
     tiles_y = (height + TILE_SIZE - 1) // TILE_SIZE
     counts = torch.empty((n,), device=means2d.device, dtype=torch.int32)
-    nat.call("gs_tile_counts", nat.ptr(means2d), nat.ptr(radii), n, width, height, nat.ptr(counts), nat.stream())
-    sorted_ids, tile_ranges = bin_with_counts(means2d, radii, depths, counts, width, height)
+    if conics is None:
+        nat.call("gs_tile_counts", nat.ptr(means2d), nat.ptr(radii), n, width, height, nat.ptr(counts),
+                 nat.stream())
+    else:
+        conics = nat.require_cuda("conics", conics.detach())
+        if conics.shape != (n, 3):
+            raise ValueError("conics must have shape (N, 3).")
+        nat.call("gs_tile_counts_refined", nat.ptr(means2d), nat.ptr(radii), nat.ptr(conics), n, width, height,
+                 nat.ptr(counts), nat.stream())
+    sorted_ids, tile_ranges = bin_with_counts(means2d, radii, depths, counts, width, height, conics)
     return sorted_ids, tile_ranges, tiles_x, tiles_y

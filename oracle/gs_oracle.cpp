@@ -144,6 +144,35 @@ int tile_bbox(float x, float y, float r, int W, int H, int tx, int ty, int* bb) 
   return on ? (bb[1] - bb[0] + 1) * (bb[3] - bb[2] + 1) : 0;
 }
 
+// tiles.py:96-141 for one duplicate: minimum of the conic form over the tile
+// rectangle (corners, four clipped edge minimisers, 0 inside); keep if <= 12.
+bool refine_keep(const float* co, float gx, float gy, int tile_x, int tile_y, int W, int H) {
+  const float x0 = (float)(tile_x * TILE), y0 = (float)(tile_y * TILE);
+  const float x1 = (float)std::min((tile_x + 1) * TILE, W), y1 = (float)std::min((tile_y + 1) * TILE, H);
+  const float dx_min = gs_sub(x0, gx), dx_max = gs_sub(x1, gx);
+  const float dy_min = gs_sub(y0, gy), dy_max = gs_sub(y1, gy);
+  const float a = co[0], b = co[1], c = co[2];
+  auto q = [&](float dx, float dy) {
+    return gs_add(gs_add(gs_mul(gs_mul(a, dx), dx), gs_mul(gs_mul(gs_mul(2.0f, b), dx), dy)),
+                  gs_mul(gs_mul(c, dy), dy));
+  };
+  auto clip = [](float v, float lo, float hi) { return gs_minf(gs_maxf(v, lo), hi); };
+  const bool inside = dx_min <= 0 && dx_max >= 0 && dy_min <= 0 && dy_max >= 0;
+  const float dy_at_left = clip(gs_mul(-gs_div(b, c), dx_min), dy_min, dy_max);
+  const float dy_at_right = clip(gs_mul(-gs_div(b, c), dx_max), dy_min, dy_max);
+  const float dx_at_bottom = clip(gs_mul(-gs_div(b, a), dy_min), dx_min, dx_max);
+  const float dx_at_top = clip(gs_mul(-gs_div(b, a), dy_max), dx_min, dx_max);
+  float qmin = q(dx_min, dy_min);
+  qmin = gs_minf(qmin, q(dx_min, dy_max));
+  qmin = gs_minf(qmin, q(dx_max, dy_min));
+  qmin = gs_minf(qmin, q(dx_max, dy_max));
+  qmin = gs_minf(qmin, q(dx_min, dy_at_left));
+  qmin = gs_minf(qmin, q(dx_max, dy_at_right));
+  qmin = gs_minf(qmin, q(dx_at_bottom, dy_min));
+  qmin = gs_minf(qmin, q(dx_at_top, dy_max));
+  return (inside ? 0.0f : qmin) <= 12.0f;
+}
+
 int n_threads(int requested) {
 #ifdef _OPENMP
   return requested > 0 ? requested : omp_get_max_threads();
@@ -196,14 +225,24 @@ void or_activate(const float* log_scales, const float* logits, int64_t n, float*
   for (int64_t i = 0; i < n; ++i) opac[i] = gs_sigmoidf(logits[i]);
 }
 
-// tiles.py:49-68: tiles touched per Gaussian; returns the duplicate total D.
-int64_t or_bin_count(const float* means2d, const float* radii, int64_t n, int W, int H, int32_t* counts) {
+// tiles.py:49-68 (and, with conics, the refinement's kept count
+// tiles.py:141-143): tiles per Gaussian; returns the duplicate total D.
+int64_t or_bin_count(const float* means2d, const float* radii, const float* conics, int64_t n, int W, int H,
+                     int32_t* counts) {
   const int tx = (W + TILE - 1) / TILE, ty = (H + TILE - 1) / TILE;
   int64_t total = 0;
   int bb[4];
   for (int64_t i = 0; i < n; ++i) {
-    counts[i] = tile_bbox(means2d[2 * i], means2d[2 * i + 1], radii[i], W, H, tx, ty, bb);
-    total += counts[i];
+    const int c = tile_bbox(means2d[2 * i], means2d[2 * i + 1], radii[i], W, H, tx, ty, bb);
+    int kept = c;
+    if (conics && c) {
+      kept = 0;
+      for (int y = bb[2]; y <= bb[3]; ++y)
+        for (int x = bb[0]; x <= bb[1]; ++x)
+          kept += refine_keep(conics + 3 * i, means2d[2 * i], means2d[2 * i + 1], x, y, W, H);
+    }
+    counts[i] = kept;
+    total += kept;
   }
   return total;
 }
@@ -211,8 +250,8 @@ int64_t or_bin_count(const float* means2d, const float* radii, int64_t n, int W,
 // tiles.py:77-182: duplicates in Gaussian order, key = tile * N + rank(depth)
 // with rank from a stable argsort of all depths, stable argsort of the keys,
 // per-tile [start, end) ranges with empty tiles at [0, 0).
-void or_bin_fill(const float* means2d, const float* radii, const float* depths, int64_t n, int W,
-                 int H, int64_t D, int32_t* sorted_ids, int32_t* ranges) {
+void or_bin_fill(const float* means2d, const float* radii, const float* depths, const float* conics,
+                 int64_t n, int W, int H, int64_t D, int32_t* sorted_ids, int32_t* ranges) {
   const int tx = (W + TILE - 1) / TILE, ty = (H + TILE - 1) / TILE;
   const int64_t num_tiles = (int64_t)tx * ty;
   std::vector<int32_t> gid, tid;
@@ -223,9 +262,11 @@ void or_bin_fill(const float* means2d, const float* radii, const float* depths, 
     const int c = tile_bbox(means2d[2 * i], means2d[2 * i + 1], radii[i], W, H, tx, ty, bb);
     if (!c) continue;
     const int w = bb[1] - bb[0] + 1;
-    for (int l = 0; l < c; ++l) {  // :85-89
+    for (int l = 0; l < c; ++l) {  // :85-89, then the refinement's compaction :152-163
+      const int x = bb[0] + l % w, y = bb[2] + l / w;
+      if (conics && !refine_keep(conics + 3 * i, means2d[2 * i], means2d[2 * i + 1], x, y, W, H)) continue;
       gid.push_back((int32_t)i);
-      tid.push_back((bb[2] + l / w) * tx + bb[0] + l % w);
+      tid.push_back(y * tx + x);
     }
   }
   std::vector<int64_t> order(n);

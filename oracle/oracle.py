@@ -38,9 +38,9 @@ def load() -> ctypes.CDLL:
         lib.or_eval_sh.argtypes = [c_int, P, c_int64, c_int, c_int, P, P]
         lib.or_sh_colors.argtypes = [P, c_int, P, P, c_int64, c_int, P, c_int]
         lib.or_activate.argtypes = [P, P, c_int64, P, P]
-        lib.or_bin_count.argtypes = [P, P, c_int64, c_int, c_int, P]
+        lib.or_bin_count.argtypes = [P, P, P, c_int64, c_int, c_int, P]
         lib.or_bin_count.restype = c_int64
-        lib.or_bin_fill.argtypes = [P, P, P, c_int64, c_int, c_int, c_int64, P, P]
+        lib.or_bin_fill.argtypes = [P, P, P, P, c_int64, c_int, c_int, c_int64, P, P]
         lib.or_rasterize_fwd.argtypes = [P, P, P, c_int, P, P, P, P, P, c_int, c_int, P, P, P, P, c_int]
         lib.or_rasterize_bwd.argtypes = [P, P, P, c_int, P, c_int64, P, P, P, c_int, c_int, P, P, P, P, P, P, P, P,
                                          c_int]
@@ -108,17 +108,19 @@ def sh_colors(cam, degree, means, sh, threads=0):
     return out
 
 
-def bin_gaussians(means2d, radii, depths, width, height):
-    """(counts, sorted_ids, tile_ranges, tiles_x, tiles_y) (tiles.py:19-182)."""
+def bin_gaussians(means2d, radii, depths, width, height, conics=None):
+    """(counts, sorted_ids, tile_ranges, tiles_x, tiles_y) (tiles.py:19-182);
+    ``conics`` turns on the tile refinement (tiles.py:91-164)."""
     means2d, radii, depths = _f32(means2d), _f32(radii), _f32(depths)
+    conics = None if conics is None else _f32(conics)
     n = means2d.shape[0]
     counts = np.empty((n,), np.int32)
     lib = load()
-    d = lib.or_bin_count(_p(means2d), _p(radii), n, width, height, _p(counts))
+    d = lib.or_bin_count(_p(means2d), _p(radii), _p(conics), n, width, height, _p(counts))
     tx, ty = (width + 15) // 16, (height + 15) // 16
     ids = np.empty((d,), np.int32)
     ranges = np.empty((tx * ty, 2), np.int32)
-    lib.or_bin_fill(_p(means2d), _p(radii), _p(depths), n, width, height, d, _p(ids), _p(ranges))
+    lib.or_bin_fill(_p(means2d), _p(radii), _p(depths), _p(conics), n, width, height, d, _p(ids), _p(ranges))
     return counts, ids, ranges, tx, ty
 
 
@@ -167,7 +169,7 @@ def rasterize_bwd(means2d, conics, colors, opac, ids, ranges, width, height, bac
 
 
 def render(cam, width, height, means, quats, scales, opacities, colors=None, sh=None, sh_degree=3, background=None,
-           antialias=False, with_depth=False, threads=0):
+           antialias=False, with_depth=False, threads=0, refine_tiles=False):
     """render_gaussians (render.py:29-112) on the oracle: projection,
     opacity * compensation, SH colour, binning, compositing."""
     proj = project(cam, means, quats, scales, antialias=antialias, threads=threads)
@@ -175,7 +177,8 @@ def render(cam, width, height, means, quats, scales, opacities, colors=None, sh=
     if sh is not None:
         colors = sh_colors(cam, sh_degree, means, sh, threads=threads)
     colors = _f32(colors)
-    counts, ids, ranges, tx, ty = bin_gaussians(proj["means2d"], proj["radii"], proj["depths"], width, height)
+    counts, ids, ranges, tx, ty = bin_gaussians(proj["means2d"], proj["radii"], proj["depths"], width, height,
+                                                proj["conics"] if refine_tiles else None)
     bg = np.zeros(3, np.float32) if background is None else _f32(background)
     out = rasterize_fwd(proj["means2d"], proj["conics"], colors, opac, ids, ranges, width, height, bg,
                         depths=proj["depths"] if with_depth else None, threads=threads)

@@ -371,3 +371,27 @@ def test_full_size_c2_forward_bit_exact_and_gradients():
     }
     for k, (a, b) in checks.items():
         assert rel_l2(npy(a), b) < GRAD_TOL, k
+
+
+@pytest.mark.parametrize("name", ["random300", "c0", "c2_200k"])
+def test_refined_binning_and_render_bit_exact(name):
+    cam, means, quats, scales, opac, sh, deg, aa = scene_inputs(name)
+    ref = orc.project(cam.to_native(), means, quats, scales)
+    ids, ranges, _, _ = gs.bin_gaussians(cu(ref["means2d"]), cu(ref["radii"]), cu(ref["depths"]), cam.width,
+                                         cam.height, conics=cu(ref["conics"]))
+    _, rids, rranges, _, _ = orc.bin_gaussians(ref["means2d"], ref["radii"], ref["depths"], cam.width, cam.height,
+                                               conics=ref["conics"])
+    eq(npy(ids), rids, "sorted_ids")
+    eq(npy(ranges), rranges, "tile_ranges")
+    m, q, s, o, shv = (cu(a).requires_grad_() for a in (means, quats, scales, opac, sh))
+    out = gs.render_gaussians(cam, m, q, s, o, sh=shv, sh_degree=deg, antialias=aa, refine_tiles=True)
+    fwd = orc.render(cam.to_native(), cam.width, cam.height, means, quats, scales, opac, sh=sh, sh_degree=deg,
+                     antialias=aa, refine_tiles=True)
+    for k in ("image", "final_T", "n_contrib"):
+        eq(npy(out[k]), fwd[k], k)
+    g_img = np.random.default_rng(2).normal(size=fwd["image"].shape).astype(np.float32)
+    out["image"].backward(cu(g_img))
+    _, g = orc.render_grads(cam, means, quats, scales, opac, sh=sh, sh_degree=deg, antialias=aa, grad_image=g_img,
+                            fwd=fwd)
+    for k, t in (("means", m), ("quats", q), ("scales", s), ("opacities", o), ("sh", shv)):
+        assert rel_l2(npy(t.grad), g[k]) < GRAD_TOL, k

@@ -233,3 +233,26 @@ def test_oracle_gradients_match_naive_autodiff(use_sh):
     pairs.append(("sh", shv) if use_sh else ("colors", col))
     for name, leaf in pairs:
         assert max_rel(g[name], leaf.grad.numpy()) < 1e-3, name
+
+
+def test_refined_tiles_render_matches_naive_and_drop_duplicates():
+    """test_splatting.py:225-240: rendering with refine_tiles still matches the
+    naive renderer at 1e-3; the refinement only removes duplicates."""
+    cam, means, quats, scales, opac, colors = random_scene()
+    bg = np.array([0.1, 0.2, 0.3], np.float32)
+    out = orc.render(cam.to_native(), cam.width, cam.height, means, quats, scales, opac, colors=colors,
+                     background=bg, refine_tiles=True)
+    ref = _naive(cam, means, quats, scales, opac, colors, bg)
+    np.testing.assert_allclose(out["image"], ref["image"].numpy(), atol=1e-3)
+    np.testing.assert_allclose(out["alpha"], ref["alpha"].numpy(), atol=1e-3)
+    p = _proj(cam, means, quats, scales)
+    full = orc.bin_gaussians(p["means2d"], p["radii"], p["depths"], cam.width, cam.height)
+    ref_ids, ref_ranges = full[1], full[2]
+    ids, ranges = out["sorted_ids"], out["tile_ranges"]
+    assert 0 < ids.shape[0] < ref_ids.shape[0]
+    for t in range(ranges.shape[0]):
+        kept = ids[ranges[t, 0]:ranges[t, 1]]
+        allv = list(ref_ids[ref_ranges[t, 0]:ref_ranges[t, 1]])
+        assert set(kept) <= set(allv)
+        pos = [allv.index(g) for g in kept]
+        assert pos == sorted(pos)  # same (depth, index) order
