@@ -86,6 +86,33 @@ int gs_project_backward(const gs_camera* cam, const float* means, const float* q
                         const float* g_compensation, float* g_means, float* g_quats,
                         float* g_scales, void* stream);
 
+/* Lens model for the unscented projection (cameras.py:139-173, 290-317):
+ * orthographic (fx, fy in pixels per world unit), or pinhole with
+ * n_dist = 0 (none), Brown-Conrady dist = (k1, k2, p1, p2, k3) or, with
+ * fisheye, OpenCV fisheye dist = (k1, k2, k3, k4). */
+typedef struct gs_lens {
+  int32_t orthographic;
+  int32_t fisheye;
+  int32_t n_dist;
+  float dist[5];
+} gs_lens;
+
+/* project_gaussians_ut (projection.py:149-205): six sigma points
+ * mean +- sqrt(3) * (columns of R(q) diag(s)) through the camera model,
+ * sample mean and covariance; outputs as gs_project_forward. */
+int gs_project_ut_forward(const gs_camera* cam, const gs_lens* lens, const float* means,
+                          const float* quats, const float* scales, int64_t n, float blur,
+                          int antialias, float* means2d, float* conics, float* depths,
+                          float* radii, float* compensation, void* stream);
+
+/* VJP of gs_project_ut_forward (what MLX autodiff computes through
+ * projection.py:165-205 and cameras.py:290-317); cotangents may be NULL. */
+int gs_project_ut_backward(const gs_camera* cam, const gs_lens* lens, const float* means,
+                           const float* quats, const float* scales, int64_t n, float blur,
+                           int antialias, const float* g_means2d, const float* g_conics,
+                           const float* g_depths, const float* g_compensation, float* g_means,
+                           float* g_quats, float* g_scales, void* stream);
+
 /* ------------------------------------------------------------------------ SH
  * eval_sh(degree, sh (N,K,C), dirs (N,3)) -> (N,C), offset by +0.5, unclamped.
  * Replaces src/mlx3d/splatting/sh.py:41-78.  K >= (degree+1)^2. */

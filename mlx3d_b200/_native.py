@@ -46,6 +46,12 @@ class GsCamera(ctypes.Structure):
     ]
 
 
+class GsLens(ctypes.Structure):
+    """Mirror of ``gs_lens`` in include/gsplat_b200.h."""
+
+    _fields_ = [("orthographic", c_int32), ("fisheye", c_int32), ("n_dist", c_int32), ("dist", c_float * 5)]
+
+
 class GsAdamGroup(ctypes.Structure):
     """Mirror of ``gs_adam_group`` in include/gsplat_b200.h."""
 
@@ -92,6 +98,13 @@ _SIGS = {
     "gs_bin_workspace_d_bytes": (c_size_t, [c_int64]),
     "gs_bin_begin": (c_int, [_P, _P, c_int64, _P, c_size_t, _P, _P]),
     "gs_bin_end": (c_int, [_P, _P, c_int64, c_int64, c_int, c_int, _P, c_size_t, _P, c_size_t, _P, _P, _P]),
+    "gs_project_ut_forward": (
+        c_int, [POINTER(GsCamera), POINTER(GsLens), _P, _P, _P, c_int64, c_float, c_int, _P, _P, _P, _P, _P, _P]
+    ),
+    "gs_project_ut_backward": (
+        c_int,
+        [POINTER(GsCamera), POINTER(GsLens), _P, _P, _P, c_int64, c_float, c_int, _P, _P, _P, _P, _P, _P, _P, _P],
+    ),
     "gs_tile_counts_refined": (c_int, [_P, _P, _P, c_int64, c_int, c_int, _P, _P]),
     "gs_bin_end_refined": (
         c_int, [_P, _P, _P, c_int64, c_int64, c_int, c_int, _P, c_size_t, _P, c_size_t, _P, _P, _P]

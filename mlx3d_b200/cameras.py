@@ -14,7 +14,7 @@ from dataclasses import dataclass
 
 import torch
 
-from ._native import GsCamera
+from ._native import GsCamera, GsLens
 
 __all__ = ["Camera", "look_at", "look_at_view_transform", "fov_to_focal", "focal_to_fov"]
 
@@ -63,9 +63,10 @@ def look_at_view_transform(dist=1.0, elev=0.0, azim=0.0, at=(0.0, 0.0, 0.0), up=
 
 @dataclass
 class Camera:
-    """A single pinhole camera (cameras.py:139-173).  Distortion, fisheye and
-    orthographic modes of the reference are only used by its unscented
-    projection, which this package does not provide."""
+    """A single camera (cameras.py:139-173).  ``orthographic``, ``distortion``
+    (Brown-Conrady (k1, k2, p1, p2[, k3]) or, with ``fisheye``, OpenCV fisheye
+    (k1, k2, k3, k4)) are honoured by the unscented projection
+    (``projection="ut"``); the EWA projection is pinhole, as in the reference."""
 
     R: torch.Tensor
     t: torch.Tensor
@@ -77,6 +78,9 @@ class Camera:
     height: int
     znear: float = 0.01
     zfar: float = 100.0
+    orthographic: bool = False
+    distortion: tuple | None = None
+    fisheye: bool = False
 
     @classmethod
     def from_fov(cls, fov: float, width: int, height: int, R=None, t=None, degrees: bool = True, **kw) -> "Camera":
@@ -108,6 +112,23 @@ class Camera:
 
     def world_to_camera(self, points: torch.Tensor) -> torch.Tensor:
         return points @ self.R.to(points).T + self.t.to(points)
+
+    def lens_native(self) -> GsLens:
+        """Lens model of this camera for the unscented projection."""
+        lens = GsLens()
+        lens.orthographic = int(bool(self.orthographic))
+        lens.fisheye = int(bool(self.fisheye))
+        d = tuple(self.distortion) if self.distortion is not None else ()
+        if self.fisheye:
+            d = (tuple(d) + (0.0, 0.0, 0.0, 0.0))[:4]
+        elif d:
+            if len(d) < 4:
+                raise ValueError("distortion must be (k1, k2, p1, p2[, k3])")
+            d = (tuple(d) + (0.0,))[:5]
+        lens.n_dist = len(d) if self.distortion is not None else 0
+        for i, v in enumerate(d):
+            lens.dist[i] = float(v)
+        return lens
 
     def to_native(self) -> GsCamera:
         """The float32 view of this camera the CUDA kernels consume."""

@@ -16,7 +16,7 @@ import torch
 
 from .. import _native as nat
 from ..cameras import Camera
-from .render import _check_projection, _render_fused, render_gaussian_depth, render_gaussian_features
+from .render import _check_projection, _render_composed, _render_fused, render_gaussian_depth, render_gaussian_features
 from .sh import num_sh_bases, rgb_to_sh
 
 __all__ = ["GaussianModel"]
@@ -111,6 +111,10 @@ class GaussianModel:
         kernels.  ``render_depth=True`` adds an expected ``depth`` output."""
         _check_projection(projection)
         p = self.params
+        if projection == "ut":
+            return _render_composed(camera, p["means"], p["quats"], self.scales_act, self.opacities_act, sh=self.sh,
+                                    sh_degree=self.active_sh_degree, background=background, antialias=antialias,
+                                    with_depth=render_depth)
         return _render_fused(
             camera,
             p["means"],

@@ -89,10 +89,55 @@ def project_gaussians(
     return {"means2d": means2d, "conics": conics, "depths": depths, "radii": radii, "compensation": comp}
 
 
-def project_gaussians_ut(*args, **kwargs):
-    """The reference's 3DGUT unscented projection (projection.py:149-205) is
-    not provided by this package."""
-    raise NotImplementedError("projection='ut' is not implemented in mlx3d_b200; use 'ewa'.")
+class _ProjectUT(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, means, quats, scales, cam_native, lens, blur, antialias):
+        n = means.shape[0]
+        f32 = dict(device=means.device, dtype=torch.float32)
+        means2d, conics = torch.empty((n, 2), **f32), torch.empty((n, 3), **f32)
+        depths, radii, comp = torch.empty((n,), **f32), torch.empty((n,), **f32), torch.empty((n,), **f32)
+        nat.call("gs_project_ut_forward", cam_native, lens, nat.ptr(means), nat.ptr(quats), nat.ptr(scales), n, blur,
+                 int(antialias), nat.ptr(means2d), nat.ptr(conics), nat.ptr(depths), nat.ptr(radii), nat.ptr(comp),
+                 nat.stream())
+        ctx.save_for_backward(means, quats, scales)
+        ctx.args = (cam_native, lens, blur, antialias)
+        ctx.mark_non_differentiable(radii)
+        ctx.set_materialize_grads(False)
+        return means2d, conics, depths, radii, comp
+
+    @staticmethod
+    def backward(ctx, g_means2d, g_conics, g_depths, _g_radii, g_comp):
+        means, quats, scales = ctx.saved_tensors
+        cam_native, lens, blur, antialias = ctx.args
+        g_means, g_quats, g_scales = torch.empty_like(means), torch.empty_like(quats), torch.empty_like(scales)
+        c = lambda t: None if t is None else t.contiguous()  # noqa: E731
+        nat.call("gs_project_ut_backward", cam_native, lens, nat.ptr(means), nat.ptr(quats), nat.ptr(scales),
+                 means.shape[0], blur, int(antialias), nat.ptr(c(g_means2d)), nat.ptr(c(g_conics)),
+                 nat.ptr(c(g_depths)), nat.ptr(c(g_comp)), nat.ptr(g_means), nat.ptr(g_quats), nat.ptr(g_scales),
+                 nat.stream())
+        return g_means, g_quats, g_scales, None, None, None, None
+
+
+def project_gaussians_ut(
+    camera: Camera,
+    means: torch.Tensor,
+    quats: torch.Tensor,
+    scales: torch.Tensor,
+    blur: float = 0.3,
+    antialias: bool = False,
+) -> dict[str, torch.Tensor]:
+    """3DGUT-style unscented projection (projection.py:149-205): six sigma
+    points through the camera's own model (``orthographic``, Brown-Conrady
+    or fisheye ``distortion``).  Same outputs as :func:`project_gaussians`,
+    differentiable in means, quats and scales."""
+    means = nat.require_cuda("means", means)
+    quats = nat.require_cuda("quats", quats)
+    scales = nat.require_cuda("scales", scales)
+    _check_gaussians(means, quats, scales)
+    means2d, conics, depths, radii, comp = _ProjectUT.apply(
+        means, quats, scales, camera.to_native(), camera.lens_native(), float(blur), bool(antialias) and blur > 0
+    )
+    return {"means2d": means2d, "conics": conics, "depths": depths, "radii": radii, "compensation": comp}
 
 
 def quat_scale_to_cov3d(quats: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:

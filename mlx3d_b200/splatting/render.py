@@ -16,9 +16,9 @@ import torch
 
 from .. import _native as nat
 from ..cameras import Camera
-from .projection import project_gaussians
-from .rasterize import rasterize_depth, rasterize_features
-from .sh import num_sh_bases
+from .projection import project_gaussians, project_gaussians_ut
+from .rasterize import rasterize, rasterize_depth, rasterize_features
+from .sh import eval_sh, num_sh_bases
 from .tiles import TILE_SIZE, bin_gaussians, bin_with_counts
 
 __all__ = ["render_gaussians", "render_gaussian_depth", "render_gaussian_features"]
@@ -243,10 +243,41 @@ def _render_fused(
 
 
 def _check_projection(projection: str) -> None:
-    if projection == "ut":
-        raise NotImplementedError("projection='ut' is not implemented in mlx3d_b200; use 'ewa'.")
-    if projection != "ewa":
+    if projection not in ("ewa", "ut"):
         raise ValueError("projection must be 'ewa' or 'ut'.")
+
+
+def _project(camera, means, quats, scales, projection, antialias):
+    """render.py:14-26."""
+    _check_projection(projection)
+    fn = project_gaussians if projection == "ewa" else project_gaussians_ut
+    return fn(camera, means, quats, scales, antialias=antialias)
+
+
+def _render_composed(camera, means, quats, scales, opacities, colors=None, sh=None, sh_degree=3, background=None,
+                     antialias=False, refine_tiles=False, projection="ut", with_depth=False):
+    """render_gaussians as the reference composes it (render.py:56-112), from
+    the standalone kernels: used for the unscented projection, whose sigma
+    points are not part of the fused per-Gaussian kernel."""
+    proj = _project(camera, means, quats, scales, projection, antialias)
+    opac = nat.require_cuda("opacities", opacities).reshape(-1) * proj["compensation"]
+    if sh is not None:
+        m = nat.require_cuda("means", means).detach()
+        center = camera.camera_center.to(m.device)
+        d = m - center
+        d = d / torch.clamp(torch.linalg.norm(d, dim=-1, keepdim=True), min=1e-8)
+        raw = eval_sh(sh_degree, sh, d)
+        colors = torch.where(raw > 0, raw, torch.zeros_like(raw))
+    sorted_ids, tile_ranges, tiles_x, tiles_y = bin_gaussians(
+        proj["means2d"], proj["radii"], proj["depths"], camera.width, camera.height,
+        conics=proj["conics"] if refine_tiles else None,
+    )
+    out = rasterize(proj["means2d"], proj["conics"], colors, opac, sorted_ids, tile_ranges, camera.width,
+                    camera.height, tiles_x, tiles_y, background=background)
+    if with_depth:
+        out["depth"] = rasterize_depth(proj["means2d"], proj["conics"], opac, proj["depths"], sorted_ids,
+                                       tile_ranges, camera.width, camera.height, tiles_x, tiles_y)["depth"]
+    return _extras(out, proj)
 
 
 def render_gaussians(
@@ -276,6 +307,10 @@ def render_gaussians(
     if (colors is None) == (sh is None):
         raise ValueError("Provide exactly one of `colors` or `sh`.")
     _check_projection(projection)
+    if projection == "ut":
+        return _render_composed(camera, means, quats, scales, opacities, colors=colors, sh=sh, sh_degree=sh_degree,
+                                background=background, antialias=antialias, refine_tiles=refine_tiles,
+                                with_depth=render_depth)
     return _render_fused(
         camera, means, quats, scales, opacities, colors=colors, sh=sh, sh_degree=sh_degree, background=background,
         antialias=antialias, with_depth=render_depth, refine_tiles=refine_tiles,
@@ -283,8 +318,7 @@ def render_gaussians(
 
 
 def _project_and_bin(camera, means, quats, scales, opacities, refine_tiles, antialias, projection):
-    _check_projection(projection)
-    proj = project_gaussians(camera, means, quats, scales, antialias=antialias)
+    proj = _project(camera, means, quats, scales, projection, antialias)
     opac = nat.require_cuda("opacities", opacities).reshape(-1) * proj["compensation"]
     sorted_ids, tile_ranges, tiles_x, tiles_y = bin_gaussians(
         proj["means2d"], proj["radii"], proj["depths"], camera.width, camera.height,

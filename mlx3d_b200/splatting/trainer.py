@@ -75,8 +75,6 @@ class GaussianTrainer:
                              "the Gaussian set and are not provided)")
         if self.config.projection not in {"ewa", "ut"}:
             raise ValueError("TrainerConfig.projection must be 'ewa' or 'ut'")
-        if self.config.projection == "ut":
-            raise NotImplementedError("projection='ut' is not implemented in mlx3d_b200; use 'ewa'.")
         self.scene_extent = scene_extent
         self.step_count = 0
         for k in _GROUPS:
@@ -117,6 +115,11 @@ class GaussianTrainer:
         dev = self.model.params["means"].device
         bg = torch.ones(3, device=dev) if cfg.white_background else torch.zeros(3, device=dev)
         p = self.model.params
+        if cfg.projection == "ut":
+            out = self.model.render(camera, background=bg, antialias=cfg.antialias, projection="ut")
+            loss, _, _ = l1_dssim_loss(out["image"], target, cfg.lambda_dssim)
+            (loss * scale).backward()
+            return loss.detach(), out
         out = _render_fused(
             camera, p["means"], p["quats"], p["scales"], p["opacities"], sh_dc=p["sh_dc"], sh_rest=p["sh_rest"],
             sh_degree=self.model.active_sh_degree, background=bg, antialias=cfg.antialias,
@@ -167,7 +170,7 @@ class GaussianTrainer:
     def step(self, camera: Camera, target: torch.Tensor) -> dict:
         """One optimisation step on a single view (trainer.py:319-421)."""
         cfg = self.config
-        track = cfg.densify_from <= self.step_count + 1 <= cfg.densify_until
+        track = cfg.densify_from <= self.step_count + 1 <= cfg.densify_until and cfg.projection == "ewa"
         probe = torch.zeros((self.model.num_gaussians, 2), device=target.device) if track else None
         loss, out = self._view_loss(camera, target, probe, 1.0)
         self._adam()

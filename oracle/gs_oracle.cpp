@@ -438,6 +438,106 @@ void or_rasterize_bwd(const float* means2d, const float* conics, const float* co
   }
 }
 
+// project_gaussians_ut (projection.py:149-205) with Camera.project_points
+// (cameras.py:290-317; distortion :42-50, :68-76).  `lens` = {orthographic,
+// fisheye, n_dist, dist[5]} as gs_lens.
+static void ut_project_point(const gs_camera& c, const gs_lens& L, const float* P, float* uv) {
+  float pc[3];
+  for (int i = 0; i < 3; ++i)
+    pc[i] = gs_add(gs_add(gs_add(gs_mul(P[0], c.R[3 * i]), gs_mul(P[1], c.R[3 * i + 1])), gs_mul(P[2], c.R[3 * i + 2])), c.t[i]);
+  if (L.orthographic) {
+    uv[0] = gs_add(gs_mul(c.fx, pc[0]), c.cx);
+    uv[1] = gs_add(gs_mul(c.fy, pc[1]), c.cy);
+    return;
+  }
+  const float inv = gs_div(1.0f, std::fabs(pc[2]) < 1e-8f ? 1e-8f : pc[2]);
+  float x = gs_mul(pc[0], inv), y = gs_mul(pc[1], inv);
+  if (L.n_dist > 0 && !L.fisheye) {
+    const float k1 = L.dist[0], k2 = L.dist[1], p1 = L.dist[2], p2 = L.dist[3], k3 = L.dist[4];
+    const float r2 = gs_add(gs_mul(x, x), gs_mul(y, y));
+    const float radial = gs_add(1.0f, gs_mul(r2, gs_add(k1, gs_mul(r2, gs_add(k2, gs_mul(r2, k3))))));
+    const float xd = gs_add(gs_add(gs_mul(x, radial), gs_mul(gs_mul(2.0f * p1, x), y)),
+                            gs_mul(p2, gs_add(r2, gs_mul(gs_mul(2.0f, x), x))));
+    const float yd = gs_add(gs_add(gs_mul(y, radial), gs_mul(p1, gs_add(r2, gs_mul(gs_mul(2.0f, y), y)))),
+                            gs_mul(gs_mul(2.0f * p2, x), y));
+    x = xd;
+    y = yd;
+  } else if (L.n_dist > 0) {
+    const float k1 = L.dist[0], k2 = L.dist[1], k3 = L.dist[2], k4 = L.dist[3];
+    const float r = gs_sqrt(gs_add(gs_mul(x, x), gs_mul(y, y)));
+    const float th = std::atan(r), t2 = gs_mul(th, th);
+    const float thd = gs_mul(th, gs_add(1.0f, gs_mul(t2, gs_add(k1, gs_mul(t2, gs_add(k2, gs_mul(t2, gs_add(k3, gs_mul(t2, k4)))))))));
+    const float sc = gs_div(thd, gs_maxf(r, 1e-9f));
+    x = gs_mul(x, sc);
+    y = gs_mul(y, sc);
+  }
+  uv[0] = gs_add(gs_mul(c.fx, x), c.cx);
+  uv[1] = gs_add(gs_mul(c.fy, y), c.cy);
+}
+
+void or_project_ut(const gs_camera* cam, const gs_lens* lens, const float* means, const float* quats,
+                   const float* scales, int64_t n, float blur, int aa, float* means2d, float* conics,
+                   float* depths, float* radii, float* comp) {
+  const gs_camera& c = *cam;
+  const float sq3 = gs_sqrt(3.0f), sixth = 1.0f / 6.0f;
+  for (int64_t i = 0; i < n; ++i) {
+    const float* q = quats + 4 * i;
+    const float* m = means + 3 * i;
+    const float nrm = gs_sqrt(gs_add(gs_add(gs_add(gs_mul(q[0], q[0]), gs_mul(q[1], q[1])), gs_mul(q[2], q[2])), gs_mul(q[3], q[3])));
+    const float w = gs_div(q[0], nrm), x = gs_div(q[1], nrm), y = gs_div(q[2], nrm), z = gs_div(q[3], nrm);
+    float R[3][3];  // transforms/rotations.py:30-49
+    R[0][0] = gs_sub(1.0f, gs_mul(2.0f, gs_add(gs_mul(y, y), gs_mul(z, z))));
+    R[0][1] = gs_mul(2.0f, gs_sub(gs_mul(x, y), gs_mul(w, z)));
+    R[0][2] = gs_mul(2.0f, gs_add(gs_mul(x, z), gs_mul(w, y)));
+    R[1][0] = gs_mul(2.0f, gs_add(gs_mul(x, y), gs_mul(w, z)));
+    R[1][1] = gs_sub(1.0f, gs_mul(2.0f, gs_add(gs_mul(x, x), gs_mul(z, z))));
+    R[1][2] = gs_mul(2.0f, gs_sub(gs_mul(y, z), gs_mul(w, x)));
+    R[2][0] = gs_mul(2.0f, gs_sub(gs_mul(x, z), gs_mul(w, y)));
+    R[2][1] = gs_mul(2.0f, gs_add(gs_mul(y, z), gs_mul(w, x)));
+    R[2][2] = gs_sub(1.0f, gs_mul(2.0f, gs_add(gs_mul(x, x), gs_mul(y, y))));
+    float uv[6][2];
+    for (int j = 0; j < 6; ++j) {  // offsets: columns of R diag(s), then their negatives
+      const int k = j % 3;
+      float P[3];
+      for (int r = 0; r < 3; ++r) {
+        float off = gs_mul(R[r][k], scales[3 * i + k]);
+        if (j >= 3) off = -off;
+        P[r] = gs_add(m[r], gs_mul(sq3, off));
+      }
+      ut_project_point(c, *lens, P, uv[j]);
+    }
+    float su = uv[0][0], sv = uv[0][1];
+    for (int j = 1; j < 6; ++j) { su = gs_add(su, uv[j][0]); sv = gs_add(sv, uv[j][1]); }
+    const float mu = gs_mul(su, sixth), mv = gs_mul(sv, sixth);
+    float sa = 0, sb = 0, sc = 0;
+    for (int j = 0; j < 6; ++j) {
+      const float dx = gs_sub(uv[j][0], mu), dy = gs_sub(uv[j][1], mv);
+      sa = j ? gs_add(sa, gs_mul(dx, dx)) : gs_mul(dx, dx);
+      sb = j ? gs_add(sb, gs_mul(dx, dy)) : gs_mul(dx, dy);
+      sc = j ? gs_add(sc, gs_mul(dy, dy)) : gs_mul(dy, dy);
+    }
+    const float a0 = gs_mul(sa, sixth), b = gs_mul(sb, sixth), c0 = gs_mul(sc, sixth);
+    const float a = gs_add(a0, blur), cc = gs_add(c0, blur);
+    const float det = gs_sub(gs_mul(a, cc), gs_mul(b, b));
+    const float ds = gs_maxf(det, 1e-12f);
+    conics[3 * i] = gs_div(cc, ds);
+    conics[3 * i + 1] = gs_div(-b, ds);
+    conics[3 * i + 2] = gs_div(a, ds);
+    float cp = 1.0f;
+    if (aa && blur > 0.0f) cp = gs_sqrt(gs_div(gs_maxf(gs_sub(gs_mul(a0, c0), gs_mul(b, b)), 0.0f), ds));
+    const float mid = gs_mul(0.5f, gs_add(a, cc));
+    const float lam1 = gs_add(mid, gs_sqrt(gs_maxf(gs_sub(gs_mul(mid, mid), det), 0.01f)));
+    const float rad = std::ceil(gs_mul(3.0f, gs_sqrt(gs_maxf(lam1, 0.0f))));
+    const float zc = gs_add(gs_add(gs_add(gs_mul(m[0], c.R[6]), gs_mul(m[1], c.R[7])), gs_mul(m[2], c.R[8])), c.t[2]);
+    const bool valid = zc > c.znear && det > 0.0f;
+    means2d[2 * i] = mu;
+    means2d[2 * i + 1] = mv;
+    depths[i] = zc;
+    radii[i] = valid ? rad : 0.0f;
+    comp[i] = valid ? cp : 0.0f;
+  }
+}
+
 // The shared exponential, exported so tests can check it against libm.
 float or_expf(float x) { return gs_expf(x); }
 

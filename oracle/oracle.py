@@ -44,6 +44,7 @@ def load() -> ctypes.CDLL:
         lib.or_rasterize_fwd.argtypes = [P, P, P, c_int, P, P, P, P, P, c_int, c_int, P, P, P, P, c_int]
         lib.or_rasterize_bwd.argtypes = [P, P, P, c_int, P, c_int64, P, P, P, c_int, c_int, P, P, P, P, P, P, P, P,
                                          c_int]
+        lib.or_project_ut.argtypes = [P, P, P, P, P, c_int64, c_float, c_int, P, P, P, P, P]
         lib.or_expf.argtypes = [c_float]
         lib.or_expf.restype = c_float
         _lib = lib
@@ -88,6 +89,19 @@ def project(cam, means, quats, scales, blur=0.3, antialias=False, threads=0):
     }
     load().or_project(ctypes.byref(cam), _p(means), _p(quats), _p(scales), n, blur, int(antialias and blur > 0),
                       *(_p(out[k]) for k in ("means2d", "conics", "depths", "radii", "compensation")), threads)
+    return out
+
+
+def project_ut(camera, means, quats, scales, blur=0.3, antialias=False):
+    """project_gaussians_ut (projection.py:149-205) for a mlx3d_b200 Camera."""
+    means, quats, scales = _f32(means), _f32(quats), _f32(scales)
+    n = means.shape[0]
+    out = {k: np.empty(s, np.float32) for k, s in (("means2d", (n, 2)), ("conics", (n, 3)), ("depths", (n,)),
+                                                  ("radii", (n,)), ("compensation", (n,)))}
+    cam, lens = camera.to_native(), camera.lens_native()
+    load().or_project_ut(ctypes.byref(cam), ctypes.byref(lens), _p(means), _p(quats), _p(scales), n, blur,
+                         int(antialias and blur > 0),
+                         *(_p(out[k]) for k in ("means2d", "conics", "depths", "radii", "compensation")))
     return out
 
 

@@ -194,3 +194,60 @@ def adam_update(p, g, m, v, lr, b1=0.9, b2=0.999, eps=1e-15):
     v = f(b2) * v + f(1.0 - b2) * (g * g)
     p = p - (f(lr) * m) / (np.sqrt(v) + f(eps))
     return p.astype(np.float32), m.astype(np.float32), v.astype(np.float32)
+
+
+def project_points(camera, pts, eps=1e-8):
+    """Camera.project_points (cameras.py:290-317, distortion :42-76)."""
+    R, t = camera.R.to(pts.dtype), camera.t.to(pts.dtype)
+    pc = pts @ R.T + t
+    z = pc[..., 2]
+    if camera.orthographic:
+        return torch.stack([camera.fx * pc[..., 0] + camera.cx, camera.fy * pc[..., 1] + camera.cy], -1)
+    inv = 1.0 / torch.where(z.abs() < eps, torch.full_like(z, eps), z)
+    x, y = pc[..., 0] * inv, pc[..., 1] * inv
+    d = camera.distortion
+    if d is not None and not camera.fisheye:
+        k1, k2, p1, p2 = d[0], d[1], d[2], d[3]
+        k3 = d[4] if len(d) > 4 else 0.0
+        r2 = x * x + y * y
+        radial = 1.0 + r2 * (k1 + r2 * (k2 + r2 * k3))
+        x, y = (x * radial + 2.0 * p1 * x * y + p2 * (r2 + 2.0 * x * x),
+                y * radial + p1 * (r2 + 2.0 * y * y) + 2.0 * p2 * x * y)
+    elif d is not None:
+        k1, k2, k3, k4 = (list(d) + [0.0] * 4)[:4]
+        r = torch.sqrt(x * x + y * y)
+        th = torch.atan(r)
+        th2 = th * th
+        thd = th * (1.0 + th2 * (k1 + th2 * (k2 + th2 * (k3 + th2 * k4))))
+        sc = thd / torch.clamp(r, min=1e-9)
+        x, y = x * sc, y * sc
+    return torch.stack([camera.fx * x + camera.cx, camera.fy * y + camera.cy], -1)
+
+
+def project_ut(camera, means, quats, scales, blur=0.3, antialias=False):
+    """project_gaussians_ut (projection.py:149-205)."""
+    q = quats / torch.linalg.norm(quats, dim=-1, keepdim=True)
+    w, x, y, z = q.unbind(-1)
+    R = torch.stack([1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y),
+                     2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x),
+                     2 * (x * z - w * y), 2 * (y * z + w * x), 1 - 2 * (x * x + y * y)], -1).reshape(-1, 3, 3)
+    sqrt_cov = R * scales[:, None, :]
+    offsets = torch.cat([sqrt_cov.transpose(1, 2), -sqrt_cov.transpose(1, 2)], dim=1)
+    sigma = means[:, None, :] + 3.0 ** 0.5 * offsets
+    xy = project_points(camera, sigma.reshape(-1, 3)).reshape(means.shape[0], 6, 2)
+    m2 = xy.mean(dim=1)
+    d = xy - m2[:, None, :]
+    a0 = (d[..., 0] * d[..., 0]).mean(1)
+    b = (d[..., 0] * d[..., 1]).mean(1)
+    c0 = (d[..., 1] * d[..., 1]).mean(1)
+    a, c = a0 + blur, c0 + blur
+    det = a * c - b * b
+    ds = torch.clamp(det, min=1e-12)
+    conics = torch.stack([c / ds, -b / ds, a / ds], -1)
+    comp = torch.sqrt(torch.clamp(a0 * c0 - b * b, min=0.0) / ds) if (antialias and blur > 0) else torch.ones_like(det)
+    mid = 0.5 * (a + c)
+    radii = torch.ceil(3.0 * torch.sqrt(torch.clamp(mid + torch.sqrt(torch.clamp(mid * mid - det, min=0.01)), min=0)))
+    zc = (means @ camera.R.to(means.dtype).T + camera.t.to(means.dtype))[:, 2]
+    valid = (zc > camera.znear) & (det > 0)
+    return {"means2d": m2, "conics": conics, "depths": zc, "radii": torch.where(valid, radii, 0 * radii).detach(),
+            "compensation": torch.where(valid, comp, 0 * comp)}

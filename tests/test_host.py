@@ -58,7 +58,7 @@ def test_render_argument_validation():
         gs.render_gaussian_features(cam, z, torch.zeros(2, 4), z, torch.zeros(2), torch.zeros(2))
     with pytest.raises(ValueError, match="same first dimension"):
         gs.render_gaussian_features(cam, z, torch.zeros(2, 4), z, torch.zeros(2), torch.zeros(1, 4))
-    with pytest.raises(NotImplementedError):
+    with pytest.raises(ValueError, match="CUDA"):
         gs.render_gaussians(cam, z, torch.zeros(2, 4), z, torch.zeros(2), colors=z, projection="ut")
 
 

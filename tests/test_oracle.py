@@ -256,3 +256,55 @@ def test_refined_tiles_render_matches_naive_and_drop_duplicates():
         assert set(kept) <= set(allv)
         pos = [allv.index(g) for g in kept]
         assert pos == sorted(pos)  # same (depth, index) order
+
+
+def _ut_cams():
+    base = Camera.look_at(eye=(0, 0, -3.0), at=(0, 0, 0), fov=60.0, width=128, height=128)
+    mk = lambda **kw: Camera(R=base.R, t=base.t, fx=base.fx, fy=base.fy, cx=base.cx, cy=base.cy,  # noqa: E731
+                             width=base.width, height=base.height, **kw)
+    return base, mk
+
+
+def test_ut_projection_respects_camera_distortion():
+    """test_splatting.py:75-97 on the oracle."""
+    base, mk = _ut_cams()
+    cam = mk(distortion=(-0.35, 0.12, 0.002, -0.001))
+    means = np.array([[0.75, 0.45, 0.0]], np.float32)
+    quats = np.array([[1.0, 0, 0, 0]], np.float32)
+    scales = np.full((1, 3), 1e-4, np.float32)
+    ut = orc.project_ut(cam, means, quats, scales)
+    center = torch_ref.project_points(cam, torch.tensor(means)).numpy()
+    ewa = orc.project(cam.to_native(), means, quats, scales)
+    np.testing.assert_allclose(ut["means2d"], center, atol=1e-3)
+    assert np.abs(ewa["means2d"] - center).max() > 0.25
+    assert ut["radii"][0] > 0
+
+
+def test_ut_projection_close_to_ewa_for_pinhole_small_gaussians():
+    """test_splatting.py:100-111 on the oracle."""
+    cam = Camera.look_at(eye=(0, 0, -3.0), at=(0, 0, 0), fov=55.0, width=96, height=64)
+    means = np.array([[0.0, 0.0, 0.0], [0.2, -0.1, 0.3]], np.float32)
+    quats = np.array([[1.0, 0, 0, 0], [0.9, 0.1, 0.2, 0.3]], np.float32)
+    scales = np.full((2, 3), 1e-3, np.float32)
+    ut = orc.project_ut(cam, means, quats, scales)
+    ewa = orc.project(cam.to_native(), means, quats, scales)
+    np.testing.assert_allclose(ut["means2d"], ewa["means2d"], atol=1e-3)
+    np.testing.assert_allclose(ut["conics"], ewa["conics"], rtol=0.05)
+
+
+@pytest.mark.parametrize("lens", ["pinhole", "brown", "fisheye", "ortho"])
+def test_ut_oracle_matches_autograd_restatement(lens):
+    base, mk = _ut_cams()
+    cam = {"pinhole": base, "brown": mk(distortion=(-0.2, 0.05, 0.001, -0.002, 0.01)),
+           "fisheye": mk(distortion=(0.05, -0.01, 0.002, 0.0), fisheye=True),
+           "ortho": Camera(R=base.R, t=base.t, fx=40.0, fy=40.0, cx=64.0, cy=64.0, width=128, height=128,
+                           orthographic=True)}[lens]
+    rng = np.random.default_rng(3)
+    means = (rng.normal(size=(64, 3)) * 0.5).astype(np.float32)
+    quats = rng.normal(size=(64, 4)).astype(np.float32)
+    scales = np.exp(rng.normal(size=(64, 3)) * 0.3 - 3).astype(np.float32)
+    a = orc.project_ut(cam, means, quats, scales, antialias=True)
+    b = torch_ref.project_ut(cam, t64(means), t64(quats), t64(scales), antialias=True)
+    np.testing.assert_allclose(a["means2d"], b["means2d"].numpy(), atol=1e-3)
+    np.testing.assert_allclose(a["conics"], b["conics"].numpy(), rtol=1e-3, atol=1e-4)
+    np.testing.assert_allclose(a["compensation"], b["compensation"].numpy(), atol=1e-4)
