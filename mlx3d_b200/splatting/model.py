@@ -151,6 +151,23 @@ class GaussianModel:
                                         features, background=background, normalize=normalize,
                                         antialias=antialias, projection=projection)
 
+    def save_ply(self, path: str) -> None:
+        """Save in the standard 3DGS PLY layout (model.py:338-361)."""
+        from ..ply import save_gaussians_ply
+
+        save_gaussians_ply(path, self.params)
+
+    @classmethod
+    def load_ply(cls, path: str, sh_degree: int = 3, device="cuda") -> "GaussianModel":
+        """Load a 3DGS PLY checkpoint (model.py:363-392); the active SH degree
+        is the file's degree."""
+        from ..ply import load_gaussians_ply
+
+        params, degree = load_gaussians_ply(path, sh_degree, device=device)
+        model = cls(params, sh_degree=degree)
+        model.active_sh_degree = degree
+        return model
+
     def one_up_sh_degree(self) -> None:
         if self.active_sh_degree < self.sh_degree:
             self.active_sh_degree += 1
