@@ -50,60 +50,64 @@ def parse_args():
 
 # --------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons every 200 ms while active."""
+    """Samples SM clock and clock-event (throttle) reasons every 10 ms through
+    NVML while the timed region runs (read-only queries)."""
 
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clocks-event reason bits
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown",
+               0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown"}
 
     def __init__(self, gpu_index: int):
         self.gpu = gpu_index
-        self.proc = None
-        self.lines: list[str] = []
+        self.sm: list[float] = []
+        self.reasons: set[str] = set()
+        self.max_mhz = None
+        self.stop = threading.Event()
         self.thread = None
+        self.nv = None
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
-                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.thread = threading.Thread(target=self._read, daemon=True)
+            import pynvml as nv
+
+            nv.nvmlInit()
+            vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+            idx = int(vis.split(",")[self.gpu]) if vis else self.gpu
+            self.h = nv.nvmlDeviceGetHandleByIndex(idx)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.h, nv.NVML_CLOCK_SM))
+            self.nv = nv
+            self.thread = threading.Thread(target=self._run, daemon=True)
             self.thread.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+        except Exception:  # no NVML: clocks stay unreported
+            self.nv = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _sample(self):
+        nv = self.nv
+        self.sm.append(float(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM)))
+        try:
+            bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+        except AttributeError:
+            bits = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+        for b, name in self.REASONS.items():
+            if bits & b:
+                self.reasons.add(name)
+
+    def _run(self):
+        self._sample()
+        while not self.stop.wait(0.01):
+            self._sample()
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-            if self.thread is not None:
-                self.thread.join(timeout=2)
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=2)
+            self._sample()
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            parts = [x.strip() for x in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[5:9]):
-                if val.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        sm = self.sm
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(sm)}
 
 
 # ------------------------------------------------------------ distributed glue
@@ -355,6 +359,23 @@ def run_ours(args, world, rank, local):
     }
     if world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(scene, cam, cfg, steps=1)
+        if rank == 0 and cam is scene.cameras[0]:
+            # FP32 roofline of the two compositors (instruction-bound, not HBM-bound):
+            # algorithmic work per SURVEY 8(d) — 21 FLOP per pixel-Gaussian pair the
+            # reference's forward loop evaluates, 45 FLOP per pair it composites
+            # (backward) — counted exactly by the oracle on this frame, over the
+            # kernels' live CUDA-event times.  Peak: nominal dense FP32,
+            # 148 SMs x 128 lanes x 2 FLOP x 1.965 GHz.
+            n_eval, n_comp = cpu_baseline.last_pairs
+            peak = 148 * 128 * 2 * 1.965e9 / 1e12
+            rf = {}
+            for k, flops in (("gs_rasterize_forward", 21.0 * n_eval), ("gs_rasterize_backward", 45.0 * n_comp)):
+                t = stages.get(k)
+                if t:
+                    ach = flops / (t * 1e-3) / 1e12
+                    rf[k] = {"achieved": round(ach, 2), "peak": round(peak, 1), "unit": "TFLOP/s",
+                             "frac": round(ach / peak, 4), "peak_source": "nominal", "flops": flops}
+            line["roofline_fp32"] = dict(rf, pairs_evaluated=n_eval, pairs_composited=n_comp)
     return line
 
 
@@ -383,8 +404,9 @@ def cpu_baseline(scene, cam, cfg, steps=1):
     torch.set_num_threads(cores)
     t0 = time.perf_counter()
     for _ in range(steps):
-        _oracle_frame(scene, cam, cfg)
+        fwd = _oracle_frame(scene, cam, cfg)
     ms = (time.perf_counter() - t0) * 1000.0 / steps
+    cpu_baseline.last_pairs = (fwd["pairs_evaluated"], fwd["pairs_composited"])
     return {"value": round(ms, 1), "unit": "ms/frame", "cores": cores, "kind": "port",
             "sample": f"{steps} full frame(s) of the same workload: C++ oracle (OpenMP, {cores} threads) for "
                       "projection, SH, binning and both compositors; torch float64 autograd (CPU) for the "

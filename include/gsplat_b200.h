@@ -178,6 +178,10 @@ int gs_tile_counts(const float* means2d, const float* radii, int64_t n, int widt
 size_t gs_bin_workspace_n_bytes(int64_t n);
 size_t gs_bin_workspace_d_bytes(int64_t d);
 
+/* D = sum of tiles_touched into *d_total (device), on its own: lets the host
+ * read D back while gs_bin_begin's depth sort is still running. */
+int gs_bin_total(const int32_t* tiles_touched, int64_t n, int64_t* d_total, void* stream);
+
 int gs_bin_begin(const float* depths, const int32_t* tiles_touched, int64_t n, void* ws_n,
                  size_t ws_n_bytes, int64_t* d_total, void* stream);
 

@@ -16,6 +16,7 @@
 //
 // Each radix pass is reduce-then-scan (per-block digit histograms, a scan
 // over them, a stable scatter), so no block ever waits on another block.
+#include <algorithm>
 #include <utility>
 
 #include "gs_common.cuh"
@@ -160,6 +161,16 @@ k_rs_downsweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__
 }
 
 // --------------------------------------------------------- binning kernels
+// Sum of the tiles-touched counts (= D) into *total (zeroed by the caller).
+__global__ void k_count_total(const int32_t* __restrict__ counts, int64_t n,
+                              unsigned long long* __restrict__ total) {
+  unsigned long long s = 0;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x)
+    s += (unsigned)counts[i];
+  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  if ((threadIdx.x & 31) == 0 && s) atomicAdd(total, s);
+}
+
 __global__ void k_depth_keys(const float* __restrict__ depths, const int32_t* __restrict__ counts,
                              int64_t n, uint32_t* __restrict__ keys, int32_t* __restrict__ vals) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -504,6 +515,20 @@ static int bin_end_impl(const float* means2d, const float* radii, const float* c
 extern "C" {
 
 size_t gs_bin_workspace_n_bytes(int64_t n) { return NLayout(n < 0 ? 0 : n).total; }
+
+int gs_bin_total(const int32_t* tiles_touched, int64_t n, int64_t* d_total, void* stream) {
+  clear_error();
+  cudaStream_t s = as_stream(stream);
+  if (!d_total) return set_error(GS_ERR_INVALID_ARG, "d_total is NULL");
+  if (n < 0) return set_error(GS_ERR_INVALID_ARG, "n must be >= 0");
+  if (cudaMemsetAsync(d_total, 0, sizeof(int64_t), s) != cudaSuccess)
+    return set_error(GS_ERR_CUDA, "cudaMemsetAsync failed");
+  if (n == 0) return GS_OK;
+  if (!tiles_touched) return set_error(GS_ERR_INVALID_ARG, "tiles_touched is NULL");
+  const unsigned grid = (unsigned)std::min<int64_t>(ceil_div(n, 256), 148 * 4);
+  k_count_total<<<grid, 256, 0, s>>>(tiles_touched, n, reinterpret_cast<unsigned long long*>(d_total));
+  return check_launch("k_count_total");
+}
 size_t gs_bin_workspace_d_bytes(int64_t d) { return DLayout(d < 0 ? 0 : d).total; }
 
 int gs_bin_begin(const float* depths, const int32_t* tiles_touched, int64_t n, void* ws_n,

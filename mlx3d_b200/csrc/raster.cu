@@ -176,7 +176,9 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
                                       __ldg(a.conics + 3 * g + 2), o);
         const float pf = power_floor(o);
         s_xy[t] = m;
-        s_co[t] = co;
+        // -a/2 and -c/2: scaling by a power of two commutes with rounding, so
+        // (-a/2 dx) dx + (-c/2 dy) dy == -0.5 ((a dx) dx + (c dy) dy) exactly
+        s_co[t] = make_float4(-0.5f * co.x, co.y, -0.5f * co.z, co.w);
         s_pf[t] = pf;
         s_qm[t] = quad_mask(m, co, pf, cull_box(m, co, pf), tile, a.tiles_x);
 #pragma unroll
@@ -196,14 +198,14 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
       const float4 co = s_co[j];
       const float pf = s_pf[j];
       const float dx = gs_sub(m.x, pxf);
-      const float adxdx = gs_mul(gs_mul(co.x, dx), dx);
+      const float adxdx = gs_mul(gs_mul(co.x, dx), dx);  // co.x = -a/2
       const float bdx = gs_mul(co.y, dx);
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         if (done[p]) continue;
         const float dy = gs_sub(m.y, pyf[p]);
         const float power =
-            gs_sub(gs_mul(-0.5f, gs_add(adxdx, gs_mul(gs_mul(co.z, dy), dy))), gs_mul(bdx, dy));
+            gs_sub(gs_add(adxdx, gs_mul(gs_mul(co.z, dy), dy)), gs_mul(bdx, dy));
         if (power > 0.0f || power < pf) continue;
         const float alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, gs_expf(power)));
         if (alpha < GS_ALPHA_MIN) continue;
@@ -381,7 +383,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
                                       __ldg(a.conics + 3 * gid + 2), o);
         const float pf = power_floor(o);
         s_xy[threadIdx.x] = m;
-        s_co[threadIdx.x] = co;
+        s_co[threadIdx.x] = make_float4(-0.5f * co.x, co.y, -0.5f * co.z, co.w);  // see the forward
         s_pf[threadIdx.x] = pf;
         const float4 bb = cull_box(m, co, pf);
         s_bb[threadIdx.x] = bb;
@@ -411,9 +413,8 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
       for (int p = 0; p < 2; ++p) {
         if (!(col_in && b0 + j < last[p] && pyf[p] >= bb.z && pyf[p] <= bb.w)) continue;
         const float dx = gs_sub(m.x, pxf), dy = gs_sub(m.y, pyf[p]);
-        const float power = gs_sub(
-            gs_mul(-0.5f, gs_add(gs_mul(gs_mul(co.x, dx), dx), gs_mul(gs_mul(co.z, dy), dy))),
-            gs_mul(gs_mul(co.y, dx), dy));
+        const float power = gs_sub(gs_add(gs_mul(gs_mul(co.x, dx), dx), gs_mul(gs_mul(co.z, dy), dy)),
+                                   gs_mul(gs_mul(co.y, dx), dy));
         if (power > 0.0f || power < pf) continue;
         const float G = gs_expf(power);
         const float alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, G));
@@ -432,8 +433,8 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         R[p] += cd * aT;
         const float dL_dG = co.w * dL_dalpha;
         const float gdx = G * dx, gdy = G * dy;
-        gv[0] -= (gdx * co.x + gdy * co.y) * dL_dG;
-        gv[1] -= (gdy * co.z + gdx * co.y) * dL_dG;
+        gv[0] -= (gdx * (-2.0f * co.x) + gdy * co.y) * dL_dG;
+        gv[1] -= (gdy * (-2.0f * co.z) + gdx * co.y) * dL_dG;
         gv[2] -= 0.5f * gdx * dx * dL_dG;
         gv[3] -= gdx * dy * dL_dG;
         gv[4] -= 0.5f * gdy * dy * dL_dG;

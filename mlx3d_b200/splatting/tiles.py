@@ -8,6 +8,8 @@ total D is read back to the host once per call to size the outputs.
 
 from __future__ import annotations
 
+import threading
+
 import torch
 
 from .. import _native as nat
@@ -15,6 +17,18 @@ from .. import _native as nat
 TILE_SIZE = 16
 
 __all__ = ["TILE_SIZE", "bin_gaussians", "bin_with_counts"]
+
+_PINNED: dict = {}
+
+
+def _pinned_d() -> torch.Tensor:
+    """A pinned host int64 for the duplicate count (one per thread and device)."""
+    key = (threading.get_ident(), torch.cuda.current_device())
+    t = _PINNED.get(key)
+    if t is None:
+        t = torch.empty((1,), dtype=torch.int64).pin_memory()
+        _PINNED[key] = t
+    return t
 
 
 def bin_with_counts(
@@ -36,10 +50,19 @@ def bin_with_counts(
     lib = nat.load()
     s = nat.stream()
     ws_n = torch.empty((max(1, lib.gs_bin_workspace_n_bytes(n)),), device=dev, dtype=torch.uint8)
-    d_total = torch.empty((1,), device=dev, dtype=torch.int64)
+    d_total = torch.empty((2,), device=dev, dtype=torch.int64)
+    # D first (it does not depend on the depth order): its copy to the host
+    # overlaps the depth sort, so the host sizes the D buffers and queues the
+    # rest of the frame while the GPU is still sorting.
+    nat.call("gs_bin_total", nat.ptr(tiles_touched), n, nat.ptr(d_total), s)
+    d_host = _pinned_d()
+    d_host.copy_(d_total[:1], non_blocking=True)
+    ready = torch.cuda.Event()
+    ready.record()
     nat.call("gs_bin_begin", nat.ptr(depths), nat.ptr(tiles_touched), n, nat.ptr(ws_n), ws_n.numel(),
-             nat.ptr(d_total), s)
-    d = int(d_total.item())
+             nat.ptr(d_total[1:]), s)
+    ready.synchronize()
+    d = int(d_host[0])
     ws_d = torch.empty((max(1, lib.gs_bin_workspace_d_bytes(d)),), device=dev, dtype=torch.uint8)
     sorted_ids = torch.empty((d,), device=dev, dtype=torch.int32)
     tile_ranges = torch.empty((tiles_x * tiles_y, 2), device=dev, dtype=torch.int32)

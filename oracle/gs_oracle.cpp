@@ -297,9 +297,12 @@ void or_bin_fill(const float* means2d, const float* radii, const float* depths, 
 void or_rasterize_fwd(const float* means2d, const float* conics, const float* colors, int C,
                       const float* opac, const float* depths, const int32_t* ids,
                       const int32_t* ranges, const float* bg, int W, int H, float* image,
-                      float* final_T, int32_t* n_contrib, float* depth, int threads) {
+                      float* final_T, int32_t* n_contrib, float* depth, int threads, int64_t* stats) {
+  // stats (optional): [0] pixel-Gaussian pairs evaluated (loop iterations up
+  // to termination), [1] pairs composited.
   const int tx = (W + TILE - 1) / TILE, ty = (H + TILE - 1) / TILE;
-#pragma omp parallel for schedule(dynamic, 4) num_threads(n_threads(threads))
+  int64_t n_eval = 0, n_comp = 0;
+#pragma omp parallel for schedule(dynamic, 4) num_threads(n_threads(threads)) reduction(+ : n_eval, n_comp)
   for (int tile = 0; tile < tx * ty; ++tile) {
     const int start = ranges[2 * tile], end = ranges[2 * tile + 1];
     std::vector<float> acc(C > 0 ? C : 1);
@@ -312,6 +315,7 @@ void or_rasterize_fwd(const float* means2d, const float* conics, const float* co
         std::fill(acc.begin(), acc.end(), 0.0f);
         int last = 0;
         for (int k = start; k < end; ++k) {
+          ++n_eval;
           const int g = ids[k];
           const float dx = gs_sub(means2d[2 * g], pxf), dy = gs_sub(means2d[2 * g + 1], pyf);
           const float* co = conics + 3 * g;
@@ -322,6 +326,7 @@ void or_rasterize_fwd(const float* means2d, const float* conics, const float* co
           if (alpha < 1.0f / 255.0f) continue;
           const float next_T = gs_mul(T, gs_sub(1.0f, alpha));
           if (next_T < 1e-4f) break;
+          ++n_comp;
           const float w = gs_mul(alpha, T);
           for (int ch = 0; ch < C; ++ch) acc[ch] = gs_add(acc[ch], gs_mul(colors[(int64_t)g * C + ch], w));
           if (depth) dacc = gs_add(dacc, gs_mul(depths[g], w));
@@ -337,6 +342,10 @@ void or_rasterize_fwd(const float* means2d, const float* conics, const float* co
           depth[pid] = al > 1e-6f ? gs_div(dacc, al) : 0.0f;
         }
       }
+  }
+  if (stats) {
+    stats[0] = n_eval;
+    stats[1] = n_comp;
   }
 }
 

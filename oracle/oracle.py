@@ -41,7 +41,7 @@ def load() -> ctypes.CDLL:
         lib.or_bin_count.argtypes = [P, P, P, c_int64, c_int, c_int, P]
         lib.or_bin_count.restype = c_int64
         lib.or_bin_fill.argtypes = [P, P, P, P, c_int64, c_int, c_int, c_int64, P, P]
-        lib.or_rasterize_fwd.argtypes = [P, P, P, c_int, P, P, P, P, P, c_int, c_int, P, P, P, P, c_int]
+        lib.or_rasterize_fwd.argtypes = [P, P, P, c_int, P, P, P, P, P, c_int, c_int, P, P, P, P, c_int, P]
         lib.or_rasterize_bwd.argtypes = [P, P, P, c_int, P, c_int64, P, P, P, c_int, c_int, P, P, P, P, P, P, P, P,
                                          c_int]
         lib.or_project_ut.argtypes = [P, P, P, P, P, c_int64, c_float, c_int, P, P, P, P, P]
@@ -151,9 +151,11 @@ def rasterize_fwd(means2d, conics, colors, opac, ids, ranges, width, height, bac
     final_T = np.empty((height, width), np.float32)
     n_contrib = np.empty((height, width), np.int32)
     depth = np.empty((height, width), np.float32) if depths is not None else None
+    stats = np.zeros(2, np.int64)
     load().or_rasterize_fwd(_p(means2d), _p(conics), _p(colors), c, _p(opac), _p(dz), _p(ids), _p(ranges), _p(bg),
-                            width, height, _p(image), _p(final_T), _p(n_contrib), _p(depth), threads)
-    out = {"final_T": final_T, "alpha": 1.0 - final_T, "n_contrib": n_contrib}
+                            width, height, _p(image), _p(final_T), _p(n_contrib), _p(depth), threads, _p(stats))
+    out = {"final_T": final_T, "alpha": 1.0 - final_T, "n_contrib": n_contrib,
+           "pairs_evaluated": int(stats[0]), "pairs_composited": int(stats[1])}
     if c:
         out["image"] = image
     if depth is not None:
