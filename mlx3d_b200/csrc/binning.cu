@@ -41,11 +41,22 @@ k_rs_upsweep(const uint32_t* __restrict__ keys, int64_t n, int shift, uint32_t* 
   const int warp = threadIdx.x >> 5;
   for (int i = threadIdx.x; i < RS_WARPS * RS_RADIX; i += RS_THREADS) (&h[0][0])[i] = 0;
   __syncthreads();
-  const int64_t base = (int64_t)blockIdx.x * RS_TILE;
-#pragma unroll 4
-  for (int i = threadIdx.x; i < RS_TILE; i += RS_THREADS) {
-    const int64_t idx = base + i;
-    if (idx < n) atomicAdd(&h[warp][(__ldg(keys + idx) >> shift) & 255u], 1u);
+  // RS_ITEMS consecutive keys per thread, loaded as 16-byte vectors (key
+  // buffers are 256-byte aligned and blocks start at multiples of RS_TILE),
+  // all loads issued before the shared-memory counting.
+  const int64_t first = (int64_t)blockIdx.x * RS_TILE + (int64_t)threadIdx.x * RS_ITEMS;
+  uint32_t k[RS_ITEMS];
+  if (first + RS_ITEMS <= n) {
+#pragma unroll
+    for (int v = 0; v < RS_ITEMS / 4; ++v) {
+      const uint4 q = __ldg(reinterpret_cast<const uint4*>(keys + first) + v);
+      k[4 * v] = q.x; k[4 * v + 1] = q.y; k[4 * v + 2] = q.z; k[4 * v + 3] = q.w;
+    }
+#pragma unroll
+    for (int it = 0; it < RS_ITEMS; ++it) atomicAdd(&h[warp][(k[it] >> shift) & 255u], 1u);
+  } else {
+    for (int it = 0; it < RS_ITEMS; ++it)
+      if (first + it < n) atomicAdd(&h[warp][(__ldg(keys + first + it) >> shift) & 255u], 1u);
   }
   __syncthreads();
   const int d = threadIdx.x;
