@@ -416,8 +416,16 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         const float power = gs_sub(gs_add(gs_mul(gs_mul(co.x, dx), dx), gs_mul(gs_mul(co.z, dy), dy)),
                                    gs_mul(gs_mul(co.y, dx), dy));
         if (power > 0.0f || power < pf) continue;
-        const float G = gs_expf(power);
-        const float alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, G));
+        // The gradient needs e^power only to float accuracy, but the skip
+        // decision alpha < 1/255 must be the forward's: take the hardware
+        // exponential (relative error ~1e-7) and redo it exactly only when
+        // alpha lands within 1e-5 of the threshold.
+        float G = __expf(power);
+        float alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, G));
+        if (fabsf(alpha - GS_ALPHA_MIN) < 1e-5f * GS_ALPHA_MIN) {
+          G = gs_expf(power);
+          alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, G));
+        }
         if (alpha < GS_ALPHA_MIN) continue;
         any = true;
         const float ra = __fdividef(1.0f, 1.0f - alpha);
@@ -431,14 +439,18 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         }
         const float dL_dalpha = T[p] * cd - (R[p] + tail[p]) * ra;
         R[p] += cd * aT;
-        const float dL_dG = co.w * dL_dalpha;
-        const float gdx = G * dx, gdy = G * dy;
-        gv[0] -= (gdx * (-2.0f * co.x) + gdy * co.y) * dL_dG;
-        gv[1] -= (gdy * (-2.0f * co.z) + gdx * co.y) * dL_dG;
-        gv[2] -= 0.5f * gdx * dx * dL_dG;
-        gv[3] -= gdx * dy * dL_dG;
-        gv[4] -= 0.5f * gdy * dy * dL_dG;
-        gv[5] += G * dL_dalpha;
+        // d power / d(mean, conic) with u = G dL/dG (co.x = -a/2, co.z = -c/2):
+        //   means2d: -u (a dx + b dy), -u (b dx + c dy)
+        //   conic:   -u dx^2 / 2, -u dx dy, -u dy^2 / 2
+        const float gdl = G * dL_dalpha;
+        const float u = co.w * gdl;
+        const float ux = u * dx, uy = u * dy;
+        gv[0] += 2.0f * co.x * ux - co.y * uy;
+        gv[1] += 2.0f * co.z * uy - co.y * ux;
+        gv[2] -= 0.5f * ux * dx;
+        gv[3] -= ux * dy;
+        gv[4] -= 0.5f * uy * dy;
+        gv[5] += gdl;
       }
       if (!__any_sync(0xffffffffu, any)) continue;
 #pragma unroll
