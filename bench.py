@@ -186,20 +186,17 @@ def run_ours(args, world, rank, local):
     model = GaussianModel(params, sh_degree=3)
     model.active_sh_degree = cfg.sh_degree
     target = scene.target(view=rank, device=dev)
-    plist = list(params.values())
 
     from mlx3d_b200.distributed import allreduce_gradients
 
-    def allreduce_grads():
-        allreduce_gradients(plist)
-
-    def step():
-        for p in plist:
+    def step(model_=model, target_=target):
+        pl = list(model_.params.values())
+        for p in pl:
             p.grad = None
-        out = model.render(cam, antialias=cfg.antialias)
-        loss = (out["image"] - target).abs().mean()
+        out = model_.render(cam, antialias=cfg.antialias)
+        loss = (out["image"] - target_).abs().mean()
         loss.backward()
-        allreduce_grads()
+        allreduce_gradients(pl)
         return loss
 
     def barrier():
@@ -281,27 +278,40 @@ def run_ours(args, world, rank, local):
     # ---- end to end through the public API with host buffers
     e2e = None
     if not args.no_e2e:
+        # Every step copies all of its inputs (the Gaussians' parameters and
+        # the target image) from pinned host memory and reads the loss back;
+        # the copy of step k+1 runs on a copy stream under step k's kernels
+        # (HostStager double-buffers the device side).
+        from mlx3d_b200.staging import HostStager
+
         host = {k: v.detach().cpu().pin_memory() for k, v in params.items()}
-        host_target = target.cpu().pin_memory()
+        host["target"] = target.cpu().pin_memory()
         loss_host = torch.empty((), dtype=torch.float32).pin_memory()
-        h2d = sum(v.numel() * 4 for v in host.values()) + host_target.numel() * 4
+        stager = HostStager(host, dev, requires_grad=tuple(params))
+        h2d = stager.h2d_bytes()
+        models = []
+        for slot in stager.slots:
+            m = GaussianModel({k: slot[k] for k in params}, sh_degree=3)
+            m.active_sh_degree = cfg.sh_degree
+            models.append(m)
 
-        def e2e_step():
-            with torch.no_grad():
-                for k, p in params.items():
-                    p.copy_(host[k], non_blocking=True)
-                target.copy_(host_target, non_blocking=True)
-            loss = step()
-            loss_host.copy_(loss.detach(), non_blocking=True)
+        def e2e_run(k_steps):
+            stager.copy_stream.wait_stream(torch.cuda.current_stream())
+            stager.prefetch(host)
+            for k in range(k_steps):
+                if k + 1 < k_steps:
+                    stager.prefetch(host)
+                i, slot = stager.acquire()
+                loss = step(models[i], slot["target"])
+                loss_host.copy_(loss.detach(), non_blocking=True)
+                stager.release(i)
 
-        for _ in range(max(1, args.warmup // 2)):
-            e2e_step()
+        e2e_run(max(3, args.warmup))
         torch.cuda.synchronize()
         barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
-        for _ in range(args.steps):
-            e2e_step()
+        e2e_run(args.steps)
         e1.record()
         torch.cuda.synchronize()
         te = torch.tensor([e0.elapsed_time(e1) / args.steps], device=dev)
