@@ -130,6 +130,32 @@ GS_HD float gs_expf(float x) {
   return gs_mul(gs_mul(p, gs_pow2i(k + 64)), gs_pow2i(-64));
 }
 
+// e^x for -87 <= x <= 0: the operations of gs_expf's fast path, with n =
+// rint(x log2e) taken by the round-to-nearest-even addition of 1.5 * 2^23
+// (exact for |x log2e| < 2^22; the sum's low mantissa bits hold n) instead
+// of rintf and a float-to-int conversion.  Bit-identical to gs_expf on that
+// interval (tests/test_oracle.py checks every float in it).
+GS_HD float gs_expf_nonpos(float x) {
+  const float kLog2e = 1.44269502162933349609375f;
+  const float kLn2Hi = 0.693147182464599609375f;
+  const float kLn2Lo = -1.904654299957768e-09f;
+  const float kShift = 12582912.0f;  // 1.5 * 2^23
+  const float s = gs_add(gs_mul(x, kLog2e), kShift);
+  const float n = gs_sub(s, kShift);
+  const int k = (int)(gs_float_to_bits(s) - 0x4B400000u);
+  float r = gs_fma(-n, kLn2Hi, x);
+  r = gs_fma(-n, kLn2Lo, r);
+  float p = 1.98412698412698412e-4f;
+  p = gs_fma(p, r, 1.38888888888888889e-3f);
+  p = gs_fma(p, r, 8.33333333333333333e-3f);
+  p = gs_fma(p, r, 4.16666666666666667e-2f);
+  p = gs_fma(p, r, 1.66666666666666667e-1f);
+  p = gs_fma(p, r, 0.5f);
+  p = gs_fma(p, r, 1.0f);
+  p = gs_fma(p, r, 1.0f);
+  return gs_mul(p, gs_pow2i(k));
+}
+
 // Logistic sigmoid 1 / (1 + e^-x) on top of gs_expf (model activations,
 // src/mlx3d/splatting/model.py:120-122).
 GS_HD float gs_sigmoidf(float x) { return gs_div(1.0f, gs_add(1.0f, gs_expf(-x))); }

@@ -26,9 +26,11 @@ struct RasterArgs {
 // Opacity-aware early reject: alpha = min(0.99, o*e^p) < 1/255 is certain
 // when p < ln(1/(255 o)) - margin.  The margin (1e-3) is far above the error
 // of gs_expf (< 2 ulp), so the skip never changes a decision of the exact
-// test; it only avoids evaluating the exponential.
+// test; it only avoids evaluating the exponential.  The floor is at least
+// -87 (o e^-87 < 1/255 for every o <= 1), which keeps the arguments that
+// reach the exponential inside gs_expf_nonpos's domain.
 __device__ __forceinline__ float power_floor(float o) {
-  return o > 0.0f ? -logf(255.0f * o) - 1e-3f : INFINITY;
+  return o > 0.0f ? fmaxf(-logf(255.0f * o) - 1e-3f, -87.0f) : INFINITY;
 }
 
 // Conservative pixel-space box (xmin, xmax, ymin, ymax) around every pixel
@@ -118,8 +120,9 @@ __device__ __forceinline__ int quad_mask(float2 m, float4 co, float pf, float4 b
 
 // Forward compositor.  One CTA of 128 threads per tile (TilePixels layout);
 // each thread owns two pixels, so every staged Gaussian is read from shared
-// memory once per two pixels, and a warp skips Gaussians whose cull_box
-// misses its quadrant.  Front-to-back blending per pixel exactly as
+// memory once per two pixels.  After staging a batch, each warp compacts
+// the indices of the Gaussians whose quad_mask covers its quadrant into a
+// list (ballot + prefix popcount) and loops over that list only.  Front-to-back blending per pixel exactly as
 // rasterize.py:74-87: skip power > 0, skip alpha < 1/255, stop before
 // compositing once T would drop below 1e-4.  The CTA leaves the tile when
 // all of its pixels have stopped (counted at every batch boundary).
@@ -135,6 +138,7 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
   __shared__ int s_qm[kFwdBatch];     // quad_mask
   __shared__ float s_col[NC][kFwdBatch];
   __shared__ float s_z[DEPTH ? kFwdBatch : 1];
+  __shared__ short s_list[kFwdThreads / 32][kFwdBatch];
 
   const int tile = blockIdx.x;
   const int warp = threadIdx.x >> 5;
@@ -189,11 +193,20 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
     }
     __syncthreads();
     const int bs = min(kFwdBatch, num - b0);
-    for (int j = 0; j < bs; ++j) {
+    // this warp's hits of the batch, in order
+    int cnt = 0;
+    const int lane = threadIdx.x & 31;
+    for (int c = 0; c < bs; c += 32) {
+      const int jj = c + lane;
+      const bool hit = jj < bs && ((s_qm[jj] >> warp) & 1);
+      const unsigned bal = __ballot_sync(0xffffffffu, hit);
+      if (hit) s_list[warp][cnt + __popc(bal & ((1u << lane) - 1u))] = (short)jj;
+      cnt += __popc(bal);
+    }
+    __syncwarp();
+    for (int t = 0; t < cnt; ++t) {
       if (done[0] && done[1]) break;
-      // Whole-warp skip only: a per-pixel test saves nothing under SIMT
-      // unless every lane skips, which this test already catches.
-      if (!((s_qm[j] >> warp) & 1)) continue;
+      const int j = s_list[warp][t];
       const float2 m = s_xy[j];
       const float4 co = s_co[j];
       const float pf = s_pf[j];
@@ -207,7 +220,8 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
         const float power =
             gs_sub(gs_add(adxdx, gs_mul(gs_mul(co.z, dy), dy)), gs_mul(bdx, dy));
         if (power > 0.0f || power < pf) continue;
-        const float alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, gs_expf(power)));
+        // fminf == gs_minf here: neither operand is NaN
+        const float alpha = fminf(GS_ALPHA_MAX, gs_mul(co.w, gs_expf_nonpos(power)));
         if (alpha < GS_ALPHA_MIN) continue;
         const float next_T = gs_mul(T[p], gs_sub(1.0f, alpha));
         if (next_T < GS_T_MIN) {
@@ -317,6 +331,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
   // stores for one Gaussian in eight different banks
   __shared__ float s_gw[kBwdWarps][NV][BATCH + 1];
   __shared__ int s_max_last;
+  __shared__ short s_blist[kBwdWarps][BATCH];
 
   const int tile = blockIdx.x;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -398,8 +413,18 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
     __syncthreads();
     const int bs = min(BATCH, num - b0);
     const int jtop = min(bs, wmax - b0) - 1;
-    for (int j = jtop; j >= 0; --j) {
-      if (!((s_qm[j] >> warp) & 1)) continue;  // the whole warp's quadrant is outside
+    // this warp's hits among entries 0..jtop, replayed back to front
+    int cnt = 0;
+    for (int c = 0; c <= jtop; c += 32) {
+      const int jj = c + lane;
+      const bool hit = jj <= jtop && ((s_qm[jj] >> warp) & 1);
+      const unsigned bal = __ballot_sync(0xffffffffu, hit);
+      if (hit) s_blist[warp][cnt + __popc(bal & ((1u << lane) - 1u))] = (short)jj;
+      cnt += __popc(bal);
+    }
+    __syncwarp();
+    for (int t = cnt - 1; t >= 0; --t) {
+      const int j = s_blist[warp][t];
       const float4 bb = s_bb[j];
       const bool col_in = pxf >= bb.x && pxf <= bb.y;
       const float4 co = s_co[j];

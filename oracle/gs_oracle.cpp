@@ -550,4 +550,19 @@ void or_project_ut(const gs_camera* cam, const gs_lens* lens, const float* means
 // The shared exponential, exported so tests can check it against libm.
 float or_expf(float x) { return gs_expf(x); }
 
+// Number of floats x in [-87, 0] (and -0) where gs_expf_nonpos(x) differs
+// bitwise from gs_expf(x): an exhaustive check of the compositors' exponential.
+int64_t or_expf_nonpos_mismatches(void) {
+  const int64_t lo = 0x80000000LL, hi = (int64_t)gs_float_to_bits(-87.0f);
+  int64_t bad = 0;
+#pragma omp parallel for reduction(+ : bad) schedule(static)
+  for (int64_t b = lo; b <= hi; ++b) {
+    const float x = gs_bits_to_float((uint32_t)b);
+    bad += gs_float_to_bits(gs_expf_nonpos(x)) != gs_float_to_bits(gs_expf(x));
+  }
+  // +0 as well
+  bad += gs_float_to_bits(gs_expf_nonpos(0.0f)) != gs_float_to_bits(gs_expf(0.0f));
+  return bad;
+}
+
 }  // extern "C"

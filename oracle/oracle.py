@@ -47,6 +47,8 @@ def load() -> ctypes.CDLL:
         lib.or_project_ut.argtypes = [P, P, P, P, P, c_int64, c_float, c_int, P, P, P, P, P]
         lib.or_expf.argtypes = [c_float]
         lib.or_expf.restype = c_float
+        lib.or_expf_nonpos_mismatches.argtypes = []
+        lib.or_expf_nonpos_mismatches.restype = ctypes.c_int64
         _lib = lib
     return _lib
 
@@ -65,6 +67,12 @@ def _p(a):
 
 def expf(x: float) -> float:
     return load().or_expf(x)
+
+
+def expf_nonpos_mismatches() -> int:
+    """Exhaustive count of floats in [-87, 0] where the compositors'
+    exponential differs bitwise from gs_expf."""
+    return int(load().or_expf_nonpos_mismatches())
 
 
 def activate(log_scales, logits):

@@ -38,6 +38,10 @@ def test_expf_within_two_ulp():
         assert abs(got - ref) <= 2 * float(ulp), (x, got, ref)
 
 
+def test_compositor_exponential_is_bitwise_gs_expf_on_its_domain():
+    assert orc.expf_nonpos_mismatches() == 0
+
+
 def test_sh_dc_roundtrip_and_degree0_identity():
     rng = np.random.default_rng(1)
     rgb = rng.uniform(size=(10, 3)).astype(np.float32)
