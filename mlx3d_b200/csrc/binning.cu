@@ -14,8 +14,6 @@
 //      (ceil(log2(tiles)/8) passes, 1-2 for every configuration here).
 // Stable (tile, then depth order) == sort by tile * N + rank.
 //
-// Each radix pass is reduce-then-scan (per-block digit histograms, a scan
-// over them, a stable scatter), so no block ever waits on another block.
 #include <algorithm>
 #include <utility>
 
@@ -23,122 +21,132 @@
 
 namespace gs {
 
-constexpr int RS_THREADS = 256;
-constexpr int RS_WARPS = RS_THREADS / 32;
-constexpr int RS_ITEMS = 8;
-constexpr int RS_TILE = RS_THREADS * RS_ITEMS;  // keys per block
-constexpr int RS_RADIX = 256;
-constexpr int DEPTH_PASSES = 4;
-constexpr int MAX_TILE_PASSES = 4;
 
 // ------------------------------------------------------------- radix passes
-// Per-block histogram of one 8-bit digit; block digit counts are stored
-// digit-major (hist[d * nb + block]) and summed into gtot[d].
-__global__ void __launch_bounds__(RS_THREADS)
-k_rs_upsweep(const uint32_t* __restrict__ keys, int64_t n, int shift, uint32_t* __restrict__ hist,
-             uint32_t* __restrict__ gtot, int nb) {
-  __shared__ uint32_t h[RS_WARPS][RS_RADIX];
-  const int warp = threadIdx.x >> 5;
-  for (int i = threadIdx.x; i < RS_WARPS * RS_RADIX; i += RS_THREADS) (&h[0][0])[i] = 0;
-  __syncthreads();
-  // RS_ITEMS consecutive keys per thread, loaded as 16-byte vectors (key
-  // buffers are 256-byte aligned and blocks start at multiples of RS_TILE),
-  // all loads issued before the shared-memory counting.
-  const int64_t first = (int64_t)blockIdx.x * RS_TILE + (int64_t)threadIdx.x * RS_ITEMS;
-  uint32_t k[RS_ITEMS];
-  if (first + RS_ITEMS <= n) {
-#pragma unroll
-    for (int v = 0; v < RS_ITEMS / 4; ++v) {
-      const uint4 q = __ldg(reinterpret_cast<const uint4*>(keys + first) + v);
-      k[4 * v] = q.x; k[4 * v + 1] = q.y; k[4 * v + 2] = q.z; k[4 * v + 3] = q.w;
-    }
-#pragma unroll
-    for (int it = 0; it < RS_ITEMS; ++it) atomicAdd(&h[warp][(k[it] >> shift) & 255u], 1u);
-  } else {
-    for (int it = 0; it < RS_ITEMS; ++it)
-      if (first + it < n) atomicAdd(&h[warp][(__ldg(keys + first + it) >> shift) & 255u], 1u);
-  }
-  __syncthreads();
-  const int d = threadIdx.x;
-  uint32_t s = 0;
-#pragma unroll
-  for (int w = 0; w < RS_WARPS; ++w) s += h[w][d];
-  hist[(int64_t)d * nb + blockIdx.x] = s;
-  if (s) atomicAdd(gtot + d, s);
+// One kernel per 8-bit pass ("onesweep" structure):
+//   * the digit histograms of every pass come from the kernel that produces
+//     the keys (k_depth_keys, k_duplicate), so no pass re-reads its input to
+//     count;
+//   * a block takes the next partition of OS_TILE keys in launch order
+//     (atomic counter), ranks its keys stably by digit, publishes its
+//     per-digit counts and finds the counts of all earlier partitions by
+//     decoupled look-back over a per-partition status array;
+//   * the keys are reordered by digit in shared memory and written out in
+//     digit runs, so consecutive threads store to consecutive addresses.
+// A partition only waits on partitions with smaller indices, which were
+// taken by blocks that are already running, so every wait ends; each wait is
+// still bounded (kLookbackSpins), after which the block records the failure
+// in g_wait_failures and writes nothing.
+//
+// Status words: (tag << 32) | count, tag = 2 pass + 1 for "this partition's
+// count", 2 pass + 2 for "inclusive count of partitions 0..this one".  One
+// zeroed status array serves every pass of a sort: tags of earlier passes
+// read as "not ready".
+constexpr int OS_THREADS = 256;
+constexpr int OS_WARPS = OS_THREADS / 32;
+constexpr int OS_ITEMS = 12;
+constexpr int OS_TILE = OS_THREADS * OS_ITEMS;  // keys per partition
+constexpr int OS_RADIX = 256;
+constexpr int DEPTH_PASSES = 4;
+constexpr int MAX_TILE_PASSES = 4;
+constexpr int kLookbackSpins = 1 << 22;
+constexpr int kLookbackBatch = 8;
+
+__device__ unsigned long long g_wait_failures;
+
+__device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long long* p) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+  return v;
 }
 
-// Exclusive scan of one digit's row of block counts, offset by the counts of
-// all smaller digits.  One block per digit.
-__global__ void __launch_bounds__(RS_THREADS)
-k_rs_scan(uint32_t* __restrict__ hist, const uint32_t* __restrict__ gtot, int nb) {
-  __shared__ uint32_t warp_sums[RS_WARPS];
-  __shared__ uint32_t carry;
-  const int d = blockIdx.x;
+// Exclusive scan of one value per thread over a 256-thread block.
+__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t x, uint32_t* warp_sums,
+                                                        uint32_t& total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  // base = sum of gtot[0..d)
-  uint32_t v = threadIdx.x < d ? gtot[threadIdx.x] : 0u;
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  if (lane == 0) warp_sums[warp] = v;
+  uint32_t s = x;
+  for (int o = 1; o < 32; o <<= 1) {
+    const uint32_t t = __shfl_up_sync(0xffffffffu, s, o);
+    if (lane >= o) s += t;
+  }
+  if (lane == 31) warp_sums[warp] = s;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    uint32_t b = 0;
-    for (int w = 0; w < RS_WARPS; ++w) b += warp_sums[w];
-    carry = b;
+  uint32_t pre = 0, tot = 0;
+  for (int w = 0; w < 256 / 32; ++w) {
+    const uint32_t ws = warp_sums[w];
+    if (w < warp) pre += ws;
+    tot += ws;
   }
   __syncthreads();
-  uint32_t* row = hist + (int64_t)d * nb;
-  for (int start = 0; start < nb; start += RS_THREADS) {
-    const int i = start + threadIdx.x;
-    const uint32_t x = i < nb ? row[i] : 0u;
-    // inclusive warp scan
-    uint32_t s = x;
-    for (int o = 1; o < 32; o <<= 1) {
-      const uint32_t t = __shfl_up_sync(0xffffffffu, s, o);
-      if (lane >= o) s += t;
-    }
-    __syncthreads();  // previous iteration's readers of warp_sums / carry are done
-    if (lane == 31) warp_sums[warp] = s;
-    __syncthreads();
-    uint32_t wpre = 0, tot = 0;
-#pragma unroll
-    for (int w = 0; w < RS_WARPS; ++w) {
-      const uint32_t ws = warp_sums[w];
-      if (w < warp) wpre += ws;
-      tot += ws;
-    }
-    const uint32_t c = carry;
-    if (i < nb) row[i] = c + wpre + s - x;
-    __syncthreads();
-    if (threadIdx.x == 0) carry = c + tot;
+  total = tot;
+  return pre + s - x;
+}
+
+// Increment of h[digit] by every lane of a full warp (digit 256 = no key):
+// one shared atomic when all lanes share the digit (the common case for
+// high digits), else one per lane.
+__device__ __forceinline__ void count_digit(uint32_t* h, uint32_t digit) {
+  const uint32_t d0 = __shfl_sync(0xffffffffu, digit, 0);
+  if (__all_sync(0xffffffffu, digit == d0)) {
+    if ((threadIdx.x & 31) == 0 && d0 < 256u) atomicAdd(&h[d0], 32u);
+  } else if (digit < 256u) {
+    atomicAdd(&h[digit], 1u);
   }
 }
 
-// Stable scatter of one block of keys (and values) by one 8-bit digit.
-// Items are ranked warp by warp in index order with __match_any_sync, then
-// offset by the per-digit counts of earlier warps in the block and by the
-// block's scanned global offset.
+// Adds the per-block shared histograms h[passes][256] into ghist.
+__device__ __forceinline__ void flush_hist(const uint32_t (*h)[OS_RADIX], int passes,
+                                           uint32_t* __restrict__ ghist) {
+  for (int i = threadIdx.x; i < passes * OS_RADIX; i += blockDim.x) {
+    const uint32_t c = h[i / OS_RADIX][i % OS_RADIX];
+    if (c) atomicAdd(ghist + i, c);
+  }
+}
+
 template <bool KEYS_OUT>
-__global__ void __launch_bounds__(RS_THREADS)
-k_rs_downsweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
-               uint32_t* __restrict__ keys_out, int32_t* __restrict__ vals_out, int64_t n,
-               int shift, const uint32_t* __restrict__ hist, int nb) {
-  __shared__ uint32_t wcnt[RS_WARPS][RS_RADIX];
-  __shared__ uint32_t gbase[RS_RADIX];
+__global__ void __launch_bounds__(OS_THREADS, 3)
+k_onesweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
+           uint32_t* __restrict__ keys_out, int32_t* __restrict__ vals_out, int64_t n, int pass,
+           const uint32_t* __restrict__ ghist, unsigned long long* __restrict__ status,
+           uint32_t* __restrict__ part_ctr) {
+  __shared__ uint32_t wcnt[OS_WARPS][OS_RADIX];
+  __shared__ uint32_t s_keys[OS_TILE];
+  __shared__ int32_t s_vals[OS_TILE];
+  __shared__ uint32_t s_lstart[OS_RADIX];  // first local index of each digit
+  __shared__ uint32_t s_base[OS_RADIX];    // global index of local index 0, per digit
+  __shared__ uint32_t warp_sums[OS_WARPS];
+  __shared__ int s_part, s_fail;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int i = threadIdx.x; i < RS_WARPS * RS_RADIX; i += RS_THREADS) (&wcnt[0][0])[i] = 0;
-  gbase[threadIdx.x] = hist[(int64_t)threadIdx.x * nb + blockIdx.x];
+  const int shift = 8 * pass;
+  if (threadIdx.x == 0) {
+    s_part = (int)atomicAdd(part_ctr, 1u);
+    s_fail = 0;
+  }
+  for (int i = threadIdx.x; i < OS_WARPS * OS_RADIX; i += OS_THREADS) (&wcnt[0][0])[i] = 0;
   __syncthreads();
-  const int64_t seg = (int64_t)blockIdx.x * RS_TILE + warp * (32 * RS_ITEMS);
+  const int part = s_part;
+  const int64_t first = (int64_t)part * OS_TILE;
+  const int nvalid = (int)(n - first < OS_TILE ? n - first : OS_TILE);
+
+  // Stable ranks within the warp's OS_ITEMS x 32 keys (index order), per digit.
+  const int64_t seg = first + warp * (32 * OS_ITEMS);
   const unsigned lt = (1u << lane) - 1u;
-  uint32_t k[RS_ITEMS];
-  int32_t v[RS_ITEMS];
-  uint32_t rank[RS_ITEMS];
+  uint32_t k[OS_ITEMS];
+  int32_t v[OS_ITEMS];
+  uint32_t rank[OS_ITEMS];
 #pragma unroll
-  for (int it = 0; it < RS_ITEMS; ++it) {
+  for (int it = 0; it < OS_ITEMS; ++it) {
     const int64_t idx = seg + it * 32 + lane;
     const bool valid = idx < n;
     k[it] = valid ? __ldg(keys_in + idx) : 0u;
     v[it] = valid ? __ldg(vals_in + idx) : 0;
+  }
+#pragma unroll
+  for (int it = 0; it < OS_ITEMS; ++it) {
+    const bool valid = seg + it * 32 + lane < n;
     const uint32_t d = valid ? ((k[it] >> shift) & 255u) : 256u;
     const unsigned peers = __match_any_sync(0xffffffffu, d);
     const uint32_t cnt = valid ? wcnt[warp][d] : 0u;
@@ -148,26 +156,87 @@ k_rs_downsweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__
     rank[it] = cnt + __popc(peers & lt);
   }
   __syncthreads();
-  {
-    const int d = threadIdx.x;
-    uint32_t run = 0;
+
+  // Per digit (one thread each): block count, earlier warps' counts.
+  const int d = threadIdx.x;
+  uint32_t cnt_d = 0;
 #pragma unroll
-    for (int w = 0; w < RS_WARPS; ++w) {
-      const uint32_t t = wcnt[w][d];
-      wcnt[w][d] = run;
-      run += t;
+  for (int w = 0; w < OS_WARPS; ++w) {
+    const uint32_t t = wcnt[w][d];
+    wcnt[w][d] = cnt_d;
+    cnt_d += t;
+  }
+  const unsigned long long tagA = 2ull * pass + 1, tagP = 2ull * pass + 2;
+  unsigned long long* my = status + (int64_t)part * OS_RADIX + d;
+  st_relaxed_u64(my, ((part == 0 ? tagP : tagA) << 32) | cnt_d);
+
+  uint32_t tot;
+  const uint32_t lstart = block_exclusive_scan(cnt_d, warp_sums, tot);
+  const uint32_t gpre = block_exclusive_scan(ghist[d], warp_sums, tot);
+  s_lstart[d] = lstart;
+
+  // Decoupled look-back: counts of digit d in partitions 0..part-1, read
+  // kLookbackBatch predecessors at a time (independent loads in flight),
+  // summing "count" words until the first "inclusive" word.
+  uint32_t excl = 0;
+  if (part > 0) {
+    int j = part - 1, spins = 0;
+    bool found = false;
+    while (!found && j >= 0) {
+      unsigned long long w[kLookbackBatch];
+#pragma unroll
+      for (int q = 0; q < kLookbackBatch; ++q)
+        w[q] = j - q >= 0 ? ld_relaxed_u64(status + (int64_t)(j - q) * OS_RADIX + d) : (tagP << 32);
+      int used = 0;
+      bool stalled = false;
+#pragma unroll
+      for (int q = 0; q < kLookbackBatch; ++q) {
+        if (found || stalled) continue;
+        const unsigned long long tag = w[q] >> 32;
+        if (tag == tagP) {
+          excl += (uint32_t)w[q];
+          found = true;
+        } else if (tag == tagA) {
+          excl += (uint32_t)w[q];
+          ++used;
+        } else {
+          stalled = true;
+        }
+      }
+      j -= used;
+      if (stalled) {
+        if (++spins > kLookbackSpins) {
+          s_fail = 1;
+          break;
+        }
+        __nanosleep(32);
+      }
+    }
+    st_relaxed_u64(my, (tagP << 32) | (excl + cnt_d));
+  }
+  s_base[d] = gpre + excl - lstart;
+  __syncthreads();
+  if (s_fail) {
+    if (threadIdx.x == 0) atomicAdd(&g_wait_failures, 1ull);
+    return;
+  }
+
+  // Reorder by digit in shared memory, then write digit runs.
+#pragma unroll
+  for (int it = 0; it < OS_ITEMS; ++it) {
+    if (seg + it * 32 + lane < n) {
+      const uint32_t dd = (k[it] >> shift) & 255u;
+      const uint32_t li = s_lstart[dd] + wcnt[warp][dd] + rank[it];
+      s_keys[li] = k[it];
+      s_vals[li] = v[it];
     }
   }
   __syncthreads();
-#pragma unroll
-  for (int it = 0; it < RS_ITEMS; ++it) {
-    const int64_t idx = seg + it * 32 + lane;
-    if (idx < n) {
-      const uint32_t d = (k[it] >> shift) & 255u;
-      const uint32_t pos = gbase[d] + wcnt[warp][d] + rank[it];
-      if (KEYS_OUT) keys_out[pos] = k[it];
-      vals_out[pos] = v[it];
-    }
+  for (int i = threadIdx.x; i < nvalid; i += OS_THREADS) {
+    const uint32_t key = s_keys[i];
+    const uint32_t pos = s_base[(key >> shift) & 255u] + (uint32_t)i;
+    if (KEYS_OUT) keys_out[pos] = key;
+    vals_out[pos] = s_vals[i];
   }
 }
 
@@ -182,37 +251,34 @@ __global__ void k_count_total(const int32_t* __restrict__ counts, int64_t n,
   if ((threadIdx.x & 31) == 0 && s) atomicAdd(total, s);
 }
 
-__global__ void k_depth_keys(const float* __restrict__ depths, const int32_t* __restrict__ counts,
-                             int64_t n, uint32_t* __restrict__ keys, int32_t* __restrict__ vals) {
-  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= n) return;
-  keys[i] = counts[i] > 0 ? gs_float_to_bits(depths[i]) : 0xFFFFFFFFu;
-  vals[i] = (int32_t)i;
+// Depth keys (float bits; 0xFFFFFFFF for Gaussians touching no tile),
+// identity values, and the digit histograms of all DEPTH_PASSES passes.
+__global__ void __launch_bounds__(256)
+k_depth_keys(const float* __restrict__ depths, const int32_t* __restrict__ counts, int64_t n,
+             uint32_t* __restrict__ keys, int32_t* __restrict__ vals, uint32_t* __restrict__ ghist) {
+  __shared__ uint32_t h[DEPTH_PASSES][OS_RADIX];
+  for (int i = threadIdx.x; i < DEPTH_PASSES * OS_RADIX; i += blockDim.x) (&h[0][0])[i] = 0;
+  __syncthreads();
+  // whole warps iterate together so the digit counts can be warp-aggregated
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t b = (int64_t)blockIdx.x * blockDim.x; b < n; b += stride) {
+    const int64_t i = b + threadIdx.x;
+    const bool valid = i < n;
+    uint32_t key = 0;
+    if (valid) {
+      key = counts[i] > 0 ? gs_float_to_bits(depths[i]) : 0xFFFFFFFFu;
+      keys[i] = key;
+      vals[i] = (int32_t)i;
+    }
+#pragma unroll
+    for (int p = 0; p < DEPTH_PASSES; ++p) count_digit(h[p], valid ? (key >> (8 * p)) & 255u : 256u);
+  }
+  __syncthreads();
+  flush_hist(h, DEPTH_PASSES, ghist);
 }
 
 // Device-wide exclusive scan of counts[perm[i]] (int32), reduce-then-scan.
 constexpr int SC_THREADS = 256, SC_ITEMS = 16, SC_TILE = SC_THREADS * SC_ITEMS;
-
-__device__ __forceinline__ uint32_t block_exclusive_scan(uint32_t x, uint32_t* warp_sums,
-                                                        uint32_t& total) {
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  uint32_t s = x;
-  for (int o = 1; o < 32; o <<= 1) {
-    const uint32_t t = __shfl_up_sync(0xffffffffu, s, o);
-    if (lane >= o) s += t;
-  }
-  if (lane == 31) warp_sums[warp] = s;
-  __syncthreads();
-  uint32_t pre = 0, tot = 0;
-  for (int w = 0; w < SC_THREADS / 32; ++w) {
-    const uint32_t ws = warp_sums[w];
-    if (w < warp) pre += ws;
-    tot += ws;
-  }
-  __syncthreads();
-  total = tot;
-  return pre + s - x;
-}
 
 __global__ void __launch_bounds__(SC_THREADS)
 k_scan_reduce(const int32_t* __restrict__ counts, const int32_t* __restrict__ perm, int64_t n,
@@ -355,15 +421,111 @@ __global__ void k_tile_counts_refined(const float* __restrict__ means2d, const f
   counts[i] = c;
 }
 
-// One thread per Gaussian in depth order: write (tile id, Gaussian id) for
-// every tile of its rectangle, row-major (tiles.py:77-89), or, with REFINE,
-// for every tile the refinement keeps (tiles.py:141-163).
-template <bool REFINE>
-__global__ void k_duplicate(const float* __restrict__ means2d, const float* __restrict__ radii,
-                            const float* __restrict__ conics, const int32_t* __restrict__ perm,
-                            const uint32_t* __restrict__ offsets, int64_t n, int64_t d, int width,
-                            int height, int tiles_x, int tiles_y, uint32_t* __restrict__ tkeys,
-                            int32_t* __restrict__ tvals) {
+// Duplication (tiles.py:77-89): (tile id, Gaussian id) for every tile of
+// each Gaussian's rectangle, row-major, Gaussians in depth order.  The D
+// outputs are split into equal chunks of kDupChunk, one warp each, so a
+// Gaussian covering thousands of tiles is spread over many warps.  A warp
+// finds the Gaussian owning its first output by a 32-way search of the
+// offsets (an exclusive scan in depth order, so the owner of entry q is the
+// last Gaussian whose offset is <= q), then walks windows of 32 consecutive
+// Gaussians: entry q of a window belongs to the last lane whose start is
+// <= q (a binary search over the lanes' starts by shuffles) and is tile
+// k = q - start of that lane's rectangle.  Consecutive lanes store
+// consecutive entries.  The digit counts of the `passes` tile-sort passes
+// are taken on the way.
+constexpr int kDupChunk = 1024;
+
+template <bool HIST>
+__global__ void __launch_bounds__(256)
+k_duplicate(const float* __restrict__ means2d, const float* __restrict__ radii,
+            const int32_t* __restrict__ perm, const uint32_t* __restrict__ offsets, int64_t n,
+            int64_t d, int width, int height, int tiles_x, int tiles_y, uint32_t* __restrict__ tkeys,
+            int32_t* __restrict__ tvals, int passes, uint32_t* __restrict__ ghist) {
+  __shared__ uint32_t h[MAX_TILE_PASSES][OS_RADIX];
+  if (HIST) {
+    for (int i = threadIdx.x; i < MAX_TILE_PASSES * OS_RADIX; i += blockDim.x) (&h[0][0])[i] = 0;
+    __syncthreads();
+  }
+  const int lane = threadIdx.x & 31;
+  const int64_t wid = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int64_t q_begin = wid * kDupChunk;
+  if (q_begin < d) {
+    const int64_t q_end = min(d, q_begin + kDupChunk);
+    // owner of q_begin: last i with offsets[i] <= q_begin (offsets[0] = 0)
+    int64_t lo = 0, hi = n;
+    while (hi - lo > 32) {
+      const int64_t step = (hi - lo + 31) / 32;
+      const int64_t pidx = lo + lane * step;
+      const bool le = pidx < hi && (int64_t)offsets[pidx] <= q_begin;
+      const int last = 31 - __clz(__ballot_sync(0xffffffffu, le));  // lane 0 always qualifies
+      lo += last * step;
+      hi = min(hi, lo + step);
+    }
+    {
+      const int64_t pidx = lo + lane;
+      const bool le = pidx < hi && (int64_t)offsets[pidx] <= q_begin;
+      lo += 31 - __clz(__ballot_sync(0xffffffffu, le));
+    }
+    int64_t iw = lo;  // first Gaussian of the current window
+    int64_t q = q_begin;
+    while (q < q_end && iw < n) {
+      const int64_t i = iw + lane;
+      int x0 = 0, y0 = 0, x1 = -1, y1 = -1;
+      int32_t g = 0;
+      int64_t start = INT64_MAX, end = 0;
+      if (i < n) {
+        g = perm[i];
+        start = offsets[i];
+        end = start;
+        if (gauss_rect(reinterpret_cast<const float2*>(means2d)[g], radii[g], width, height, tiles_x,
+                       tiles_y, x0, y0, x1, y1))
+          end = start + (int64_t)(x1 - x0 + 1) * (y1 - y0 + 1);
+      }
+      const int wd = x1 - x0 + 1;
+      int64_t wend = end;
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) wend = max(wend, __shfl_xor_sync(0xffffffffu, wend, o));
+      const int64_t stop = min(q_end, wend);
+      for (int64_t qb = q; qb < stop; qb += 32) {
+        const int64_t qq = qb + lane;
+        int j = 0;
+#pragma unroll
+        for (int st = 16; st > 0; st >>= 1) {
+          const int64_t r = __shfl_sync(0xffffffffu, start, j + st);
+          if (r <= qq) j += st;
+        }
+        const int k = (int)(qq - __shfl_sync(0xffffffffu, start, j));
+        const int wj = __shfl_sync(0xffffffffu, wd, j);
+        const int x0j = __shfl_sync(0xffffffffu, x0, j), y0j = __shfl_sync(0xffffffffu, y0, j);
+        const int32_t gj = __shfl_sync(0xffffffffu, g, j);
+        const bool act = qq < stop;
+        uint32_t key = 0;
+        if (act) {
+          key = (uint32_t)((y0j + k / wj) * tiles_x + x0j + k % wj);
+          tkeys[qq] = key;
+          tvals[qq] = gj;
+        }
+        if (HIST)
+          for (int p = 0; p < passes; ++p) count_digit(h[p], act ? (key >> (8 * p)) & 255u : 256u);
+      }
+      if (stop > q) q = stop;
+      iw += 32;
+    }
+  }
+  if (HIST) {
+    __syncthreads();
+    flush_hist(h, passes, ghist);
+  }
+}
+
+// Refined duplication (tiles.py:141-163): one thread per Gaussian in depth
+// order writes the tiles the refinement keeps; the digit counts follow in
+// k_tile_hist.
+__global__ void k_duplicate_refined(const float* __restrict__ means2d, const float* __restrict__ radii,
+                                    const float* __restrict__ conics, const int32_t* __restrict__ perm,
+                                    const uint32_t* __restrict__ offsets, int64_t n, int64_t d, int width,
+                                    int height, int tiles_x, int tiles_y, uint32_t* __restrict__ tkeys,
+                                    int32_t* __restrict__ tvals) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
   const int32_t g = perm[i];
@@ -373,12 +535,28 @@ __global__ void k_duplicate(const float* __restrict__ means2d, const float* __re
   uint32_t o = offsets[i];
   for (int ty = y0; ty <= y1; ++ty)
     for (int tx = x0; tx <= x1; ++tx) {
-      if (REFINE && !refine_keep(conics + 3 * (int64_t)g, m.x, m.y, tx, ty, width, height)) continue;
+      if (!refine_keep(conics + 3 * (int64_t)g, m.x, m.y, tx, ty, width, height)) continue;
       if ((int64_t)o >= d) return;  // never past the caller's D (counts are recomputed exactly)
       tkeys[o] = (uint32_t)(ty * tiles_x + tx);
       tvals[o] = g;
       ++o;
     }
+}
+
+// Digit counts of the tile-sort passes over written keys.
+__global__ void __launch_bounds__(256)
+k_tile_hist(const uint32_t* __restrict__ tkeys, int64_t d, int passes, uint32_t* __restrict__ ghist) {
+  __shared__ uint32_t h[MAX_TILE_PASSES][OS_RADIX];
+  for (int i = threadIdx.x; i < MAX_TILE_PASSES * OS_RADIX; i += blockDim.x) (&h[0][0])[i] = 0;
+  __syncthreads();
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t b = (int64_t)blockIdx.x * blockDim.x; b < d; b += stride) {
+    const int64_t i = b + threadIdx.x;
+    const uint32_t key = i < d ? tkeys[i] : 0u;
+    for (int p = 0; p < passes; ++p) count_digit(h[p], i < d ? (key >> (8 * p)) & 255u : 256u);
+  }
+  __syncthreads();
+  flush_hist(h, passes, ghist);
 }
 
 // [start, end) of every non-empty tile from the tile-sorted keys; empty
@@ -395,11 +573,25 @@ __global__ void k_tile_ranges(const uint32_t* __restrict__ tkeys, int64_t d,
 // --------------------------------------------------------- workspace layout
 static size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
 
+// Sort bookkeeping, zeroed by one memset per sort: digit histograms of
+// every pass, the partition counters, the look-back status words.
+struct SortState {
+  size_t ghist, ctr, status, end;
+  int nb;
+  SortState(int64_t n, int passes, size_t o) {
+    nb = (int)ceil_div(n > 0 ? n : 1, OS_TILE);
+    ghist = o; o += 4 * (size_t)OS_RADIX * passes;
+    ctr = o; o += align256(4 * (size_t)passes);
+    status = o; o += align256(8 * (size_t)OS_RADIX * nb);
+    end = o;
+  }
+};
+
 struct NLayout {
-  size_t keys0, keys1, vals0, vals1, offsets, hist, gtot, bsum, total;
-  int nb_rs, nb_sc;
-  NLayout(int64_t n) {
-    nb_rs = (int)ceil_div(n > 0 ? n : 1, RS_TILE);
+  size_t keys0, keys1, vals0, vals1, offsets, bsum, total;
+  int nb_sc;
+  SortState st;
+  NLayout(int64_t n) : st(n, DEPTH_PASSES, 0) {
     nb_sc = (int)ceil_div(n > 0 ? n : 1, SC_TILE);
     size_t o = 0;
     keys0 = o; o += align256(4 * (size_t)n);
@@ -407,26 +599,23 @@ struct NLayout {
     vals0 = o; o += align256(4 * (size_t)n);
     vals1 = o; o += align256(4 * (size_t)n);
     offsets = o; o += align256(4 * (size_t)n);
-    hist = o; o += align256(4 * (size_t)RS_RADIX * nb_rs);
-    gtot = o; o += align256(4 * (size_t)RS_RADIX * DEPTH_PASSES);
     bsum = o; o += align256(8 * (size_t)nb_sc);
-    total = o;
+    st = SortState(n, DEPTH_PASSES, o);
+    total = st.end;
   }
 };
 
 struct DLayout {
-  size_t keys0, keys1, vals0, vals1, hist, gtot, total;
-  int nb_rs;
-  DLayout(int64_t d) {
-    nb_rs = (int)ceil_div(d > 0 ? d : 1, RS_TILE);
+  size_t keys0, keys1, vals0, vals1, total;
+  SortState st;
+  DLayout(int64_t d) : st(d, MAX_TILE_PASSES, 0) {
     size_t o = 0;
     keys0 = o; o += align256(4 * (size_t)d);
     keys1 = o; o += align256(4 * (size_t)d);
     vals0 = o; o += align256(4 * (size_t)d);
     vals1 = o; o += align256(4 * (size_t)d);
-    hist = o; o += align256(4 * (size_t)RS_RADIX * nb_rs);
-    gtot = o; o += align256(4 * (size_t)RS_RADIX * MAX_TILE_PASSES);
-    total = o;
+    st = SortState(d, MAX_TILE_PASSES, o);
+    total = st.end;
   }
 };
 
@@ -435,31 +624,37 @@ static T* at(void* base, size_t off) {
   return reinterpret_cast<T*>(reinterpret_cast<char*>(base) + off);
 }
 
-// Runs `passes` 8-bit LSD passes starting at bit 0 over (keys, vals); the
-// last pass writes its values to vals_final (and its keys to keys_final if
-// not NULL).  Buffers k0/v0 hold the input; k1/v1 are scratch.
-static int radix_sort(uint32_t* k0, int32_t* v0, uint32_t* k1, int32_t* v1, int64_t n, int passes,
-                      uint32_t* hist, uint32_t* gtot, int nb, uint32_t* keys_final,
-                      int32_t* vals_final, cudaStream_t s) {
-  if (cudaMemsetAsync(gtot, 0, sizeof(uint32_t) * RS_RADIX * passes, s) != cudaSuccess)
+static int zero_state(void* base, const SortState& st, cudaStream_t s) {
+  if (cudaMemsetAsync(at<char>(base, st.ghist), 0, st.end - st.ghist, s) != cudaSuccess)
     return set_error(GS_ERR_CUDA, "cudaMemsetAsync failed");
+  return GS_OK;
+}
+
+// Runs `passes` 8-bit LSD passes starting at bit 0 over (keys, vals), whose
+// digit histograms are already in the state; the last pass writes its values
+// to vals_final (and its keys to keys_final if not NULL).  Buffers k0/v0
+// hold the input; k1/v1 are scratch.
+static int radix_sort(uint32_t* k0, int32_t* v0, uint32_t* k1, int32_t* v1, int64_t n, int passes,
+                      void* base, const SortState& st, uint32_t* keys_final, int32_t* vals_final,
+                      cudaStream_t s) {
+  const uint32_t* ghist = at<uint32_t>(base, st.ghist);
+  uint32_t* ctr = at<uint32_t>(base, st.ctr);
+  unsigned long long* status = at<unsigned long long>(base, st.status);
   uint32_t* kin = k0;
   int32_t* vin = v0;
   uint32_t* kout = k1;
   int32_t* vout = v1;
   for (int p = 0; p < passes; ++p) {
-    const int shift = 8 * p;
     const bool last = p == passes - 1;
-    uint32_t* gt = gtot + RS_RADIX * p;
-    k_rs_upsweep<<<nb, RS_THREADS, 0, s>>>(kin, n, shift, hist, gt, nb);
-    k_rs_scan<<<RS_RADIX, RS_THREADS, 0, s>>>(hist, gt, nb);
     uint32_t* ko = last ? keys_final : kout;
     int32_t* vo = last ? vals_final : vout;
     if (ko)
-      k_rs_downsweep<true><<<nb, RS_THREADS, 0, s>>>(kin, vin, ko, vo, n, shift, hist, nb);
+      k_onesweep<true><<<st.nb, OS_THREADS, 0, s>>>(kin, vin, ko, vo, n, p, ghist + OS_RADIX * p, status,
+                                                     ctr + p);
     else
-      k_rs_downsweep<false><<<nb, RS_THREADS, 0, s>>>(kin, vin, nullptr, vo, n, shift, hist, nb);
-    if (int e = check_launch("radix pass", 3)) return e;
+      k_onesweep<false><<<st.nb, OS_THREADS, 0, s>>>(kin, vin, nullptr, vo, n, p, ghist + OS_RADIX * p,
+                                                      status, ctr + p);
+    if (int e = check_launch("k_onesweep")) return e;
     // The next pass reads what this one wrote.
     std::swap(kin, kout);
     std::swap(vin, vout);
@@ -504,19 +699,25 @@ static int bin_end_impl(const float* means2d, const float* radii, const float* c
   uint32_t* tk1 = at<uint32_t>(ws_d, M.keys1);
   int32_t* tv0 = at<int32_t>(ws_d, M.vals0);
   int32_t* tv1 = at<int32_t>(ws_d, M.vals1);
-  if (conics)
-    k_duplicate<true><<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(
-        means2d, radii, conics, perm, offsets, n, d, width, height, tiles_x, tiles_y, tk0, tv0);
-  else
-    k_duplicate<false><<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(
-        means2d, radii, nullptr, perm, offsets, n, d, width, height, tiles_x, tiles_y, tk0, tv0);
-  if (int e = check_launch("k_duplicate")) return e;
   const int bits = tile_bits(num_tiles);
   const int passes = bits == 0 ? 1 : (bits + 7) / 8;
+  if (passes > MAX_TILE_PASSES) return set_error(GS_ERR_CAPACITY, "too many tiles: %d", num_tiles);
+  if (int e = zero_state(ws_d, M.st, s)) return e;
+  uint32_t* ghist = at<uint32_t>(ws_d, M.st.ghist);
+  if (conics) {
+    k_duplicate_refined<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(
+        means2d, radii, conics, perm, offsets, n, d, width, height, tiles_x, tiles_y, tk0, tv0);
+    k_tile_hist<<<(unsigned)std::min<int64_t>(ceil_div(d, 256), 148 * 8), 256, 0, s>>>(tk0, d, passes, ghist);
+    if (int e = check_launch("k_duplicate_refined", 2)) return e;
+  } else {
+    const unsigned grid = (unsigned)ceil_div(d, (int64_t)kDupChunk * 8);
+    k_duplicate<true><<<grid, 256, 0, s>>>(means2d, radii, perm, offsets, n, d, width, height, tiles_x, tiles_y,
+                                           tk0, tv0, passes, ghist);
+    if (int e = check_launch("k_duplicate")) return e;
+  }
   // Final keys land in whichever key buffer the last pass does not read.
   uint32_t* kfinal = (passes % 2 == 1) ? tk1 : tk0;
-  int e = radix_sort(tk0, tv0, tk1, tv1, d, passes, at<uint32_t>(ws_d, M.hist),
-                     at<uint32_t>(ws_d, M.gtot), M.nb_rs, kfinal, sorted_ids, s);
+  int e = radix_sort(tk0, tv0, tk1, tv1, d, passes, ws_d, M.st, kfinal, sorted_ids, s);
   if (e) return e;
   k_tile_ranges<<<(unsigned)ceil_div(d, 256), 256, 0, s>>>(kfinal, d, tile_ranges);
   return check_launch("k_tile_ranges");
@@ -526,6 +727,20 @@ static int bin_end_impl(const float* means2d, const float* radii, const float* c
 extern "C" {
 
 size_t gs_bin_workspace_n_bytes(int64_t n) { return NLayout(n < 0 ? 0 : n).total; }
+
+int gs_bin_wait_failures(uint64_t* count, int reset) {
+  clear_error();
+  if (!count) return set_error(GS_ERR_INVALID_ARG, "count is NULL");
+  unsigned long long v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_wait_failures, sizeof(v));
+  if (e == cudaSuccess && reset) {
+    const unsigned long long z = 0;
+    e = cudaMemcpyToSymbol(g_wait_failures, &z, sizeof(z));
+  }
+  if (e != cudaSuccess) return set_error(GS_ERR_CUDA, "gs_bin_wait_failures: %s", cudaGetErrorString(e));
+  *count = v;
+  return GS_OK;
+}
 
 int gs_bin_total(const int32_t* tiles_touched, int64_t n, int64_t* d_total, void* stream) {
   clear_error();
@@ -561,12 +776,14 @@ int gs_bin_begin(const float* depths, const int32_t* tiles_touched, int64_t n, v
   uint32_t* k1 = at<uint32_t>(ws_n, L.keys1);
   int32_t* v0 = at<int32_t>(ws_n, L.vals0);
   int32_t* v1 = at<int32_t>(ws_n, L.vals1);
-  k_depth_keys<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(depths, tiles_touched, n, k0, v0);
+  if (int e = zero_state(ws_n, L.st, s)) return e;
+  k_depth_keys<<<(unsigned)std::min<int64_t>(ceil_div(n, 256), 148 * 8), 256, 0, s>>>(
+      depths, tiles_touched, n, k0, v0, at<uint32_t>(ws_n, L.st.ghist));
+  if (int e0 = check_launch("k_depth_keys")) return e0;
   // Pass p writes buffer (p + 1) % 2; with an even pass count the sorted
   // permutation lands in v0 (the last pass reads v1).  Keys are dropped.
   static_assert(DEPTH_PASSES % 2 == 0, "depth permutation buffer assumes an even pass count");
-  int e = radix_sort(k0, v0, k1, v1, n, DEPTH_PASSES, at<uint32_t>(ws_n, L.hist),
-                     at<uint32_t>(ws_n, L.gtot), L.nb_rs, nullptr, v0, s);
+  int e = radix_sort(k0, v0, k1, v1, n, DEPTH_PASSES, ws_n, L.st, nullptr, v0, s);
   if (e) return e;
   const int32_t* perm = v0;
   unsigned long long* bsum = at<unsigned long long>(ws_n, L.bsum);
@@ -574,7 +791,7 @@ int gs_bin_begin(const float* depths, const int32_t* tiles_touched, int64_t n, v
   k_scan_reduce<<<L.nb_sc, SC_THREADS, 0, s>>>(tiles_touched, perm, n, bsum);
   k_scan_bsums<<<1, SB_THREADS, 0, s>>>(bsum, L.nb_sc, d_total);
   k_scan_down<<<L.nb_sc, SC_THREADS, 0, s>>>(tiles_touched, perm, n, bsum, offsets);
-  return check_launch("gs_bin_begin", 4);  // k_depth_keys + 3 scan kernels
+  return check_launch("gs_bin_begin", 3);  // 3 scan kernels
 }
 
 int gs_bin_end(const float* means2d, const float* radii, int64_t n, int64_t d, int width,

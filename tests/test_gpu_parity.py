@@ -6,12 +6,14 @@ same exactly rounded float32 operation order); gradients within 1e-4
 relative L2 (atomic accumulation order is nondeterministic).
 """
 
+import ctypes
 import numpy as np
 import pytest
 import torch
 
 import oracle.oracle as orc
 from oracle import torch_ref
+from mlx3d_b200 import _native as nat
 from mlx3d_b200 import splatting as gs
 from mlx3d_b200.cameras import Camera
 from mlx3d_b200.scenes import make_scene
@@ -333,6 +335,10 @@ def test_full_size_c2_properties():
     nonempty = ranges[:, 1] > ranges[:, 0]
     assert (ranges[nonempty][1:, 0] == ranges[nonempty][:-1, 1]).all()
     assert (radii[ids] > 0).all()
+    # no radix-pass block gave up waiting for its predecessors
+    cnt = ctypes.c_uint64(0)
+    nat.call("gs_bin_wait_failures", ctypes.byref(cnt), 1)
+    assert cnt.value == 0
     # backward is linear in the output cotangent
     g = torch.randn_like(img)
     g1 = torch.autograd.grad(img, list(params.values()), g, retain_graph=True)
