@@ -154,14 +154,14 @@ def stage_bytes(stage: str, n: int, d: int, pixels: int, sh_rest_floats: int) ->
     if stage == "gs_preprocess_backward":
         return n * (12 + 16 + 12 + 4 + sh) + n * (8 + 12 + 12 + 4) + n * (12 + 16 + 12 + 4 + sh)
     if stage == "gs_bin_begin":
-        # depth keys (read depth+count, write key+val), 4 radix passes over N
-        # (read key twice, value once, write key+value), scan reading counts
+        # depth keys (read depth+count, write key+val), 4 single-kernel radix
+        # passes over N (read key+value, write key+value), scan reading counts
         # through the permutation twice and writing offsets
-        return n * 16 + 4 * n * 20 + n * (8 + 8 + 4)
+        return n * 16 + 4 * n * 16 + n * (8 + 8 + 4)
     if stage == "gs_bin_end":
         # duplication (read perm, offset, means2d, radius; write key+value per
-        # duplicate), two tile-sort passes over D, ranges (read keys)
-        return n * 20 + d * 8 + 2 * d * 20 + d * 4
+        # duplicate), two single-kernel tile-sort passes over D, ranges (read keys)
+        return n * 20 + d * 8 + 2 * d * 16 + d * 4
     if stage == "gs_rasterize_forward":
         return d * 40 + pixels * 20
     if stage == "gs_rasterize_backward":

@@ -38,9 +38,9 @@ namespace gs {
 // still bounded (kLookbackSpins), after which the block records the failure
 // in g_wait_failures and writes nothing.
 //
-// Status words: (tag << 32) | count, tag = 2 pass + 1 for "this partition's
-// count", 2 pass + 2 for "inclusive count of partitions 0..this one".  One
-// zeroed status array serves every pass of a sort: tags of earlier passes
+// Status words: pass + 1 (8 bits) | reach (24 bits) | count (32 bits): the
+// count of one digit over the `reach` partitions ending at this one.  One
+// zeroed status array serves every pass of a sort: words of earlier passes
 // read as "not ready".
 constexpr int OS_THREADS = 256;
 constexpr int OS_WARPS = OS_THREADS / 32;
@@ -50,7 +50,6 @@ constexpr int OS_RADIX = 256;
 constexpr int DEPTH_PASSES = 4;
 constexpr int MAX_TILE_PASSES = 4;
 constexpr int kLookbackSpins = 1 << 22;
-constexpr int kLookbackBatch = 8;
 
 __device__ unsigned long long g_wait_failures;
 
@@ -61,6 +60,19 @@ __device__ __forceinline__ unsigned long long ld_relaxed_u64(const unsigned long
   unsigned long long v;
   asm volatile("ld.relaxed.gpu.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
   return v;
+}
+
+// Lanes of the warp holding the same 9-bit value as this lane (values
+// 0..256; 256 marks "no key"): nine ballots, one per bit (a warp multisplit;
+// __match_any_sync takes hundreds of cycles when most lanes differ).
+__device__ __forceinline__ unsigned digit_peers(uint32_t d) {
+  unsigned m = 0xffffffffu;
+#pragma unroll
+  for (int b = 0; b < 9; ++b) {
+    const unsigned bal = __ballot_sync(0xffffffffu, (d >> b) & 1u);
+    m &= ((d >> b) & 1u) ? bal : ~bal;
+  }
+  return m;
 }
 
 // Exclusive scan of one value per thread over a 256-thread block.
@@ -107,7 +119,7 @@ __device__ __forceinline__ void flush_hist(const uint32_t (*h)[OS_RADIX], int pa
 }
 
 template <bool KEYS_OUT>
-__global__ void __launch_bounds__(OS_THREADS, 3)
+__global__ void __launch_bounds__(OS_THREADS, 4)
 k_onesweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
            uint32_t* __restrict__ keys_out, int32_t* __restrict__ vals_out, int64_t n, int pass,
            const uint32_t* __restrict__ ghist, unsigned long long* __restrict__ status,
@@ -144,16 +156,23 @@ k_onesweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ val
     k[it] = valid ? __ldg(keys_in + idx) : 0u;
     v[it] = valid ? __ldg(vals_in + idx) : 0;
   }
+  // Peer masks of all items first (independent ballots), then the running
+  // per-warp digit counters in shared memory, item by item.
+  unsigned peers[OS_ITEMS];
 #pragma unroll
   for (int it = 0; it < OS_ITEMS; ++it) {
     const bool valid = seg + it * 32 + lane < n;
-    const uint32_t d = valid ? ((k[it] >> shift) & 255u) : 256u;
-    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    peers[it] = digit_peers(valid ? ((k[it] >> shift) & 255u) : 256u);
+  }
+#pragma unroll
+  for (int it = 0; it < OS_ITEMS; ++it) {
+    const bool valid = seg + it * 32 + lane < n;
+    const uint32_t d = (k[it] >> shift) & 255u;
     const uint32_t cnt = valid ? wcnt[warp][d] : 0u;
     __syncwarp();
-    if (valid && (peers & lt) == 0u) wcnt[warp][d] = cnt + __popc(peers);
+    if (valid && (peers[it] & lt) == 0u) wcnt[warp][d] = cnt + __popc(peers[it]);
     __syncwarp();
-    rank[it] = cnt + __popc(peers & lt);
+    rank[it] = cnt + __popc(peers[it] & lt);
   }
   __syncthreads();
 
@@ -166,54 +185,38 @@ k_onesweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ val
     wcnt[w][d] = cnt_d;
     cnt_d += t;
   }
-  const unsigned long long tagA = 2ull * pass + 1, tagP = 2ull * pass + 2;
   unsigned long long* my = status + (int64_t)part * OS_RADIX + d;
-  st_relaxed_u64(my, ((part == 0 ? tagP : tagA) << 32) | cnt_d);
+  const unsigned long long tag = (unsigned long long)(pass + 1) << 56;
+  st_relaxed_u64(my, tag | (1ull << 32) | cnt_d);
 
   uint32_t tot;
   const uint32_t lstart = block_exclusive_scan(cnt_d, warp_sums, tot);
   const uint32_t gpre = block_exclusive_scan(ghist[d], warp_sums, tot);
   s_lstart[d] = lstart;
 
-  // Decoupled look-back: counts of digit d in partitions 0..part-1, read
-  // kLookbackBatch predecessors at a time (independent loads in flight),
-  // summing "count" words until the first "inclusive" word.
-  uint32_t excl = 0;
-  if (part > 0) {
-    int j = part - 1, spins = 0;
-    bool found = false;
-    while (!found && j >= 0) {
-      unsigned long long w[kLookbackBatch];
-#pragma unroll
-      for (int q = 0; q < kLookbackBatch; ++q)
-        w[q] = j - q >= 0 ? ld_relaxed_u64(status + (int64_t)(j - q) * OS_RADIX + d) : (tagP << 32);
-      int used = 0;
-      bool stalled = false;
-#pragma unroll
-      for (int q = 0; q < kLookbackBatch; ++q) {
-        if (found || stalled) continue;
-        const unsigned long long tag = w[q] >> 32;
-        if (tag == tagP) {
-          excl += (uint32_t)w[q];
-          found = true;
-        } else if (tag == tagA) {
-          excl += (uint32_t)w[q];
-          ++used;
-        } else {
-          stalled = true;
-        }
+  // Look-back by pointer jumping: the word of partition j holds the count of
+  // digit d over partitions [j - reach + 1, j]; a reader adds it and jumps
+  // to j - reach, and republishes its own, longer range after every step,
+  // so ranges roughly double per step and every block is done after about
+  // log2(partitions) reads.
+  uint32_t acc = cnt_d;  // count over [cur + 1, part]
+  int64_t cur = part - 1;
+  int spins = 0;
+  while (cur >= 0) {
+    const unsigned long long w = ld_relaxed_u64(status + cur * OS_RADIX + d);
+    if ((w & (0xFFull << 56)) != tag) {  // not yet written in this pass
+      if (++spins > kLookbackSpins) {
+        s_fail = 1;
+        break;
       }
-      j -= used;
-      if (stalled) {
-        if (++spins > kLookbackSpins) {
-          s_fail = 1;
-          break;
-        }
-        __nanosleep(32);
-      }
+      __nanosleep(32);
+      continue;
     }
-    st_relaxed_u64(my, (tagP << 32) | (excl + cnt_d));
+    acc += (uint32_t)w;
+    cur -= (int64_t)((w >> 32) & 0xFFFFFFull);
+    st_relaxed_u64(my, tag | ((unsigned long long)(part - cur) << 32) | acc);
   }
+  const uint32_t excl = acc - cnt_d;
   s_base[d] = gpre + excl - lstart;
   __syncthreads();
   if (s_fail) {
