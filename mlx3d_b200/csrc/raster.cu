@@ -58,20 +58,12 @@ __device__ __forceinline__ float4 cull_box(float2 m, float4 co, float pf) {
 // adjacent pixels (l & 7, 2 (l >> 3) + {0, 1}) of it.
 struct TilePixels {
   int px, py0;
-  float wx0, wx1, wy0, wy1;  // pixel-centre extent of the warp's quadrant
   __device__ TilePixels(int tile, int tiles_x) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int qx = (tile % tiles_x) * GS_TILE + (warp & 1) * 8;
     const int qy = (tile / tiles_x) * GS_TILE + (warp >> 1) * 8;
     px = qx + (lane & 7);
     py0 = qy + 2 * (lane >> 3);
-    wx0 = (float)qx + 0.5f;
-    wx1 = (float)qx + 7.5f;
-    wy0 = (float)qy + 0.5f;
-    wy1 = (float)qy + 7.5f;
-  }
-  __device__ bool misses(float4 bb) const {
-    return bb.y < wx0 || bb.x > wx1 || bb.w < wy0 || bb.z > wy1;
   }
 };
 
@@ -324,7 +316,6 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
   __shared__ float2 s_xy[BATCH];
   __shared__ float4 s_co[BATCH];
   __shared__ float s_pf[BATCH];
-  __shared__ float4 s_bb[BATCH];
   __shared__ int s_qm[BATCH];
   __shared__ float s_col[CMAX][BATCH];
   // per-warp gradient totals; the +1 pitch puts the eight values a warp
@@ -400,9 +391,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         s_xy[threadIdx.x] = m;
         s_co[threadIdx.x] = make_float4(-0.5f * co.x, co.y, -0.5f * co.z, co.w);  // see the forward
         s_pf[threadIdx.x] = pf;
-        const float4 bb = cull_box(m, co, pf);
-        s_bb[threadIdx.x] = bb;
-        s_qm[threadIdx.x] = quad_mask(m, co, pf, bb, tile, a.tiles_x);
+        s_qm[threadIdx.x] = quad_mask(m, co, pf, cull_box(m, co, pf), tile, a.tiles_x);
 #pragma unroll
         for (int ch = 0; ch < CMAX; ++ch)
           s_col[ch][threadIdx.x] =
@@ -425,8 +414,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
     __syncwarp();
     for (int t = cnt - 1; t >= 0; --t) {
       const int j = s_blist[warp][t];
-      const float4 bb = s_bb[j];
-      const bool col_in = pxf >= bb.x && pxf <= bb.y;
+
       const float4 co = s_co[j];
       const float2 m = s_xy[j];
       const float pf = s_pf[j];
@@ -436,7 +424,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
       bool any = false;
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        if (!(col_in && b0 + j < last[p] && pyf[p] >= bb.z && pyf[p] <= bb.w)) continue;
+        if (!(b0 + j < last[p])) continue;
         const float dx = gs_sub(m.x, pxf), dy = gs_sub(m.y, pyf[p]);
         const float power = gs_sub(gs_add(gs_mul(gs_mul(co.x, dx), dx), gs_mul(gs_mul(co.z, dy), dy)),
                                    gs_mul(gs_mul(co.y, dx), dy));
@@ -467,14 +455,17 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         // d power / d(mean, conic) with u = G dL/dG (co.x = -a/2, co.z = -c/2):
         //   means2d: -u (a dx + b dy), -u (b dx + c dy)
         //   conic:   -u dx^2 / 2, -u dx dy, -u dy^2 / 2
+        // are linear in the sums of u dx, u dy, u dx^2, u dx dy, u dy^2 over
+        // the pixels (a, b, c fixed per Gaussian): those five sums are
+        // accumulated and reduced, and the conic applied once per Gaussian.
         const float gdl = G * dL_dalpha;
         const float u = co.w * gdl;
         const float ux = u * dx, uy = u * dy;
-        gv[0] += 2.0f * co.x * ux - co.y * uy;
-        gv[1] += 2.0f * co.z * uy - co.y * ux;
-        gv[2] -= 0.5f * ux * dx;
-        gv[3] -= ux * dy;
-        gv[4] -= 0.5f * uy * dy;
+        gv[0] += ux;
+        gv[1] += uy;
+        gv[2] += ux * dx;
+        gv[3] += ux * dy;
+        gv[4] += uy * dy;
         gv[5] += gdl;
       }
       if (!__any_sync(0xffffffffu, any)) continue;
@@ -507,6 +498,14 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         hit |= v != 0.0f;
       }
       if (hit) {
+        // sums of u dx, u dy, u dx^2, u dx dy, u dy^2 -> gradients
+        const float4 cq = s_co[t];  // -a/2, b, -c/2
+        const float sx = tot[0], sy = tot[1];
+        tot[0] = 2.0f * cq.x * sx - cq.y * sy;
+        tot[1] = 2.0f * cq.z * sy - cq.y * sx;
+        tot[2] = -0.5f * tot[2];
+        tot[3] = -tot[3];
+        tot[4] = -0.5f * tot[4];
         const int gid = s_id[t];
         atomicAdd(reinterpret_cast<float2*>(g.g_means2d) + gid, make_float2(tot[0], tot[1]));
         atomicAdd(g.g_conics + 3 * gid, tot[2]);
