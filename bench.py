@@ -45,6 +45,8 @@ def parse_args():
     ap.add_argument("--views", type=int, default=None, help="override the view count (configs 3 and 4)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--sync-allreduce", action="store_true",
+                    help="multi-GPU C2: wait for each step's gradient all-reduce before the next step")
     return ap.parse_args()
 
 
@@ -187,17 +189,39 @@ def run_ours(args, world, rank, local):
     model.active_sh_degree = cfg.sh_degree
     target = scene.target(view=rank, device=dev)
 
-    from mlx3d_b200.distributed import allreduce_gradients
+    from mlx3d_b200.distributed import GradientReducer, allreduce_gradients
+
+    # Multi-GPU: the step has no optimizer, so nothing reads the summed
+    # gradient before the next view is rendered.  Step k's gradients are
+    # staged into a flat buffer at its end; their all-reduce is launched once
+    # step k+1's forward is enqueued, so it runs on NCCL's stream under step
+    # k+1's backward, and step k+1 waits for it at the end of its backward
+    # (GradientReducer, two flat buffers).  The last one is waited for before
+    # the timed region closes.  --sync-allreduce makes every step wait for
+    # its own all-reduce instead.
+    reducer = GradientReducer()
+    overlap = world > 1 and not args.sync_allreduce
 
     def step(model_=model, target_=target):
         pl = list(model_.params.values())
         for p in pl:
             p.grad = None
         out = model_.render(cam, antialias=cfg.antialias)
+        if overlap:
+            reducer.launch()
         loss = (out["image"] - target_).abs().mean()
         loss.backward()
-        allreduce_gradients(pl)
+        if overlap:
+            while reducer.in_flight():
+                reducer.finish()
+            reducer.stage(pl)
+        elif world > 1:
+            allreduce_gradients(pl)
         return loss
+
+    def drain():
+        while reducer.in_flight():
+            reducer.finish()
 
     def barrier():
         if world > 1:
@@ -205,6 +229,7 @@ def run_ours(args, world, rank, local):
 
     for _ in range(args.warmup):
         step()
+    drain()
     torch.cuda.synchronize()
     barrier()
     torch.cuda.synchronize()
@@ -215,6 +240,7 @@ def run_ours(args, world, rank, local):
         start.record()
         for _ in range(args.steps):
             step()
+        drain()
         end.record()
         torch.cuda.synchronize()
     barrier()
@@ -243,6 +269,7 @@ def run_ours(args, world, rank, local):
         prof_steps = 3
         for _ in range(prof_steps):
             step()
+        drain()
         torch.cuda.synchronize()
     finally:
         nat.call = orig_call
@@ -305,6 +332,7 @@ def run_ours(args, world, rank, local):
                 loss = step(models[i], slot["target"])
                 loss_host.copy_(loss.detach(), non_blocking=True)
                 stager.release(i)
+            drain()
 
         e2e_run(max(3, args.warmup))
         torch.cuda.synchronize()
@@ -346,7 +374,10 @@ def run_ours(args, world, rank, local):
             "views_per_step": world,
             "duplicates": d,
             "visible_gaussians": visible,
-            "parallelism": f"views sharded over {world} GPU(s); per-Gaussian gradient all-reduce (NCCL)"
+            "parallelism": (f"views sharded over {world} GPU(s); per-Gaussian gradient all-reduce (NCCL, one "
+                            f"flat 59-float-per-Gaussian buffer per step, "
+                            + ("waited for by the same step)" if args.sync_allreduce else
+                               "overlapped with the next step's render; all complete inside the timed region)"))
                            if world > 1 else "single GPU",
             "l2": "no flush: per-step working set (parameters %.0f MB + gradients + image buffers) exceeds the "
                   "126 MB L2" % (sum(v.nbytes for v in scene.params.values()) / 1e6),

@@ -12,7 +12,7 @@ from __future__ import annotations
 import torch
 import torch.distributed as dist
 
-__all__ = ["shard_views", "allreduce_gradients", "world"]
+__all__ = ["shard_views", "allreduce_gradients", "GradientReducer", "world"]
 
 
 def world() -> tuple[int, int]:
@@ -57,3 +57,73 @@ def allreduce_gradients(params: dict[str, torch.Tensor] | list[torch.Tensor], av
         n = p.grad.numel()
         p.grad.copy_(flat[off:off + n].view_as(p.grad))
         off += n
+
+
+class GradientReducer:
+    """Asynchronous form of :func:`allreduce_gradients` for pipelines in which
+    nothing reads the summed gradients before the next view has been
+    rendered (a stream of gradient evaluations without an optimizer step in
+    between, e.g. gradient statistics over many views).
+
+    ``stage`` copies the gradients into a flat buffer on the current stream;
+    ``launch`` starts the all-reduce of every staged buffer on NCCL's stream,
+    which waits for the current stream's work issued so far but does not
+    make the current stream wait (call it after enqueueing the next view's
+    forward, so the collective runs under that view's backward); ``finish``
+    makes the current stream wait for the oldest reduction (launching it
+    first if it was only staged) and returns the summed flat gradient
+    (parameter order, 59 floats per Gaussian at SH degree 3).  Two flat
+    buffers alternate, so one reduction may be in flight while the next
+    view's gradients are produced.  A training step whose optimizer needs
+    the sum before the next forward uses :func:`allreduce_gradients`."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self._bufs: list[torch.Tensor | None] = [None, None]
+        self._next = 0
+        self._pending: list[list] = []  # [work or None (staged only), buffer]
+
+    def in_flight(self) -> int:
+        return len(self._pending)
+
+    def stage(self, params: dict[str, torch.Tensor] | list[torch.Tensor]) -> None:
+        tensors = list(params.values()) if isinstance(params, dict) else list(params)
+        total = sum(p.numel() for p in tensors)
+        if len(self._pending) >= 2:
+            raise RuntimeError("GradientReducer: two reductions in flight; finish() one first")
+        i = self._next
+        self._next ^= 1
+        buf = self._bufs[i]
+        if buf is None or buf.numel() != total or buf.device != tensors[0].device:
+            buf = self._bufs[i] = torch.empty(total, dtype=tensors[0].dtype, device=tensors[0].device)
+        off = 0
+        for p in tensors:
+            n = p.numel()
+            if p.grad is None:
+                buf[off:off + n].zero_()
+            else:
+                buf[off:off + n].copy_(p.grad.reshape(-1))
+            off += n
+        self._pending.append([None, buf])
+
+    def launch(self) -> None:
+        _, ws = world()
+        for entry in self._pending:
+            if entry[0] is None:
+                entry[0] = (dist.all_reduce(entry[1], op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+                            if ws > 1 else True)
+
+    def start(self, params: dict[str, torch.Tensor] | list[torch.Tensor]) -> None:
+        """stage + launch."""
+        self.stage(params)
+        self.launch()
+
+    def finish(self) -> torch.Tensor:
+        if not self._pending:
+            raise RuntimeError("GradientReducer: nothing in flight")
+        if self._pending[0][0] is None:
+            self.launch()
+        work, buf = self._pending.pop(0)
+        if work is not True:
+            work.wait()  # the current stream waits for the collective
+        return buf

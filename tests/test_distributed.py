@@ -61,3 +61,50 @@ def test_shard_views_validates_rank():
     assert shard_views([1, 2, 3], 0, 1) == [1, 2, 3]
     with pytest.raises(ValueError):
         shard_views([1], 2, 2)
+
+
+def _reducer_worker(rank, world_size, port, results):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world_size)
+    try:
+        from mlx3d_b200.distributed import GradientReducer
+
+        red = GradientReducer()
+        params = [torch.zeros(4, requires_grad=True), torch.zeros(2, 3, requires_grad=True)]
+        sums = []
+        for step in range(5):  # two reductions in flight at most, finished in order
+            params[0].grad = torch.full((4,), float(10 * step + rank))
+            params[1].grad = torch.full((2, 3), float(step * (rank + 1)))
+            if red.in_flight() == 2:
+                sums.append(red.finish().clone())
+            if step % 2:
+                red.start(params)
+            else:  # staged only: launched by the next launch() or finish()
+                red.stage(params)
+                if step == 2:
+                    red.launch()
+        while red.in_flight():
+            sums.append(red.finish().clone())
+        results[rank] = sums
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_pipelined_gradient_reducer():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_reducer_worker, args=(r, 2, port, results)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+        for r in (0, 1):
+            sums = results[r]
+            assert len(sums) == 5
+            for step, s in enumerate(sums):
+                expect = torch.cat([torch.full((4,), float(20 * step + 1)), torch.full((6,), float(3 * step))])
+                torch.testing.assert_close(s, expect)
