@@ -235,12 +235,19 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_fwd(const PreFwdArgs a
     stage_rows<kPreBlock>(s_dc, g_dc, a.dc_stride, 3, rows);
     if (rest_len > 0) stage_rows<kPreBlock>(s_rest, g_rest, a.rest_stride, rest_len, rows);
   }
+  // This thread's own rows (quaternion, opacity) load while the staged
+  // block lands.
+  const int li = threadIdx.x;
+  const int64_t i = base + li;
+  float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+  float o_raw = 0.0f;
+  if (li < rows) {
+    q = __ldg(reinterpret_cast<const float4*>(a.quats) + i);
+    if (a.fused) o_raw = __ldg(a.opac + i);
+  }
   cp_async_wait_all();
   __syncthreads();
-  const int li = threadIdx.x;
   if (li >= rows) return;
-  const int64_t i = base + li;
-  const float4 q = __ldg(reinterpret_cast<const float4*>(a.quats) + i);
   float s0 = s_scales[li * sld + 0], s1 = s_scales[li * sld + 1], s2 = s_scales[li * sld + 2];
   if (a.flags & GS_ACT_EXP_SCALES) {
     s0 = gs_expf(s0);
@@ -258,7 +265,7 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_fwd(const PreFwdArgs a
   a.radii[i] = p.radius;
   a.comp[i] = p.comp;
   if (!a.fused) return;
-  float o = __ldg(a.opac + i);
+  float o = o_raw;
   if (a.flags & GS_ACT_SIGMOID_OPACITY) o = gs_sigmoidf(o);
   a.opac_out[i] = gs_mul(o, p.comp);
   int x0, y0, x1, y1;
@@ -435,12 +442,26 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd(const PreBwdArgs g
     stage_rows<kPreBlock>(s_dc, g_dc, a.dc_stride, 3, rows);
     if (g_rest) stage_rows<kPreBlock>(s_rest, g_rest, a.rest_stride, rest_len, rows);
   }
+  // This thread's own rows (quaternion, cotangents, opacity) load while
+  // the staged block lands.
+  const int li = threadIdx.x;
+  const int64_t i = base + li;
+  float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+  float gu = 0.f, gv = 0.f, gA = 0.f, gB = 0.f, gC = 0.f, gz = 0.f, gcomp = 0.f, o_raw = 0.f, goo = 0.f;
+  if (li < rows) {
+    q = __ldg(reinterpret_cast<const float4*>(a.quats) + i);
+    if (g.g_means2d) { gu = g.g_means2d[2 * i]; gv = g.g_means2d[2 * i + 1]; }
+    if (g.g_conics) { gA = g.g_conics[3 * i]; gB = g.g_conics[3 * i + 1]; gC = g.g_conics[3 * i + 2]; }
+    if (g.g_depths) gz = g.g_depths[i];
+    if (g.g_comp) gcomp = g.g_comp[i];
+    if (a.fused) {
+      o_raw = __ldg(a.opac + i);
+      if (g.g_opac_out) goo = g.g_opac_out[i];
+    }
+  }
   cp_async_wait_all();
   __syncthreads();
-  const int li = threadIdx.x;
   if (li < rows) {
-    const int64_t i = base + li;
-    const float4 q = __ldg(reinterpret_cast<const float4*>(a.quats) + i);
     const float r0 = s_scales[li * sld + 0], r1 = s_scales[li * sld + 1], r2 = s_scales[li * sld + 2];
     float s0 = r0, s1 = r1, s2 = r2;
     if (a.flags & GS_ACT_EXP_SCALES) {
@@ -449,17 +470,10 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd(const PreBwdArgs g
       s2 = gs_expf(r2);
     }
     const float m0 = s_means[li * mld + 0], m1 = s_means[li * mld + 1], m2 = s_means[li * mld + 2];
-    float gu = 0.f, gv = 0.f, gA = 0.f, gB = 0.f, gC = 0.f, gz = 0.f, gcomp = 0.f;
-    if (g.g_means2d) { gu = g.g_means2d[2 * i]; gv = g.g_means2d[2 * i + 1]; }
-    if (g.g_conics) { gA = g.g_conics[3 * i]; gB = g.g_conics[3 * i + 1]; gC = g.g_conics[3 * i + 2]; }
-    if (g.g_depths) gz = g.g_depths[i];
-    if (g.g_comp) gcomp = g.g_comp[i];
     if (a.fused) {
       // opacities_out = act(opacity) * compensation   (render.py:75)
-      float o_raw = __ldg(a.opac + i);
       float o = o_raw;
       if (a.flags & GS_ACT_SIGMOID_OPACITY) o = gs_sigmoidf(o_raw);
-      const float goo = g.g_opac_out ? g.g_opac_out[i] : 0.0f;
       // Compensation of this Gaussian (forward value needed for d/d opacity).
       Proj p;
       project_one(a.cam, m0, m1, m2, q.x, q.y, q.z, q.w, s0, s1, s2, a.blur, a.aa != 0, p);

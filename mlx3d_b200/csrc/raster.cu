@@ -336,10 +336,11 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
   // colour composited behind the current Gaussian, accum (rasterize.py:183),
   // and uses (c - accum) . dL/dpix * T.  Since T_i * accum_i . dL/dpix =
   // R_i / (1 - alpha_i) with R_i = sum_{j > i} (c_j . dL/dpix) alpha_j T_j,
-  // one scalar R per pixel carries the same information.
-  // tail = T_final * (bg . dL/dpix + dL/dT_final), the background term.
+  // one scalar R per pixel carries the same information; it starts at the
+  // background term T_final * (bg . dL/dpix + dL/dT_final), which enters
+  // every dL/dalpha the same way.
   bool inside[2];
-  float pyf[2], T[2], R[2], tail[2];
+  float pyf[2], T[2], R[2];
   int last[2];
   float dpix[2][CMAX];
 #pragma unroll
@@ -350,7 +351,6 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
     const int64_t pid = (int64_t)py * a.width + px;
     const float T_final = inside[p] ? a.final_T[pid] : 1.0f;
     T[p] = T_final;
-    R[p] = 0.0f;
     last[p] = inside[p] ? a.n_contrib[pid] : 0;
     float bg_dot = 0.0f;
 #pragma unroll
@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
       }
     }
     if (inside[p] && g.use_grad_final_T && g.grad_final_T) bg_dot += g.grad_final_T[pid];
-    tail[p] = T_final * bg_dot;
+    R[p] = T_final * bg_dot;
   }
 
   // Nothing at or beyond the largest n_contrib of a warp (block) matters.
@@ -450,7 +450,7 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
           cd += s_col[ch][j] * dpix[p][ch];
           gv[6 + ch] += aT * dpix[p][ch];
         }
-        const float dL_dalpha = T[p] * cd - (R[p] + tail[p]) * ra;
+        const float dL_dalpha = T[p] * cd - R[p] * ra;
         R[p] += cd * aT;
         // d power / d(mean, conic) with u = G dL/dG (co.x = -a/2, co.z = -c/2):
         //   means2d: -u (a dx + b dy), -u (b dx + c dy)
