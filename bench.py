@@ -190,6 +190,7 @@ def run_ours(args, world, rank, local):
     target = scene.target(view=rank, device=dev)
 
     from mlx3d_b200.distributed import GradientReducer, allreduce_gradients
+    from mlx3d_b200.losses import l1_loss
 
     # Multi-GPU: the step has no optimizer, so nothing reads the summed
     # gradient before the next view is rendered.  Step k's gradients are
@@ -209,7 +210,7 @@ def run_ours(args, world, rank, local):
         out = model_.render(cam, antialias=cfg.antialias)
         if overlap:
             reducer.launch()
-        loss = (out["image"] - target_).abs().mean()
+        loss = l1_loss(out["image"], target_)
         loss.backward()
         if overlap:
             while reducer.in_flight():

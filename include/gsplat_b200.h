@@ -274,6 +274,24 @@ int gs_l1_ssim_backward(const float* pred, const float* target, int height, int 
                         float lambda_dssim, float max_val, int window_size, float sigma,
                         const void* workspace, size_t workspace_bytes, float grad_scale,
                         float* grad_pred, void* stream);
+/* As gs_l1_ssim_backward with the scale read on the device,
+ * grad_sign * grad_scale[0] (an autodiff cotangent, no host read-back), and
+ * accumulate != 0 adding to grad_pred instead of overwriting it. */
+int gs_l1_ssim_backward_dev(const float* pred, const float* target, int height, int width, int channels,
+                            float lambda_dssim, int window_size, float sigma, const void* workspace,
+                            size_t workspace_bytes, const float* grad_scale, float grad_sign, int accumulate,
+                            float* grad_pred, void* stream);
+
+/* L1 photometric loss mean |pred - target| over n floats (the benchmark
+ * loss of the reference's examples/benchmark*.py and the L1 term of
+ * trainer.py:300-305): loss[0] on the device, summed in a fixed order
+ * (deterministic) through a gs_l1_workspace_bytes scratch buffer;
+ * gs_l1_backward writes grad_pred = grad_loss[0] * sign(pred - target) / n. */
+size_t gs_l1_workspace_bytes(int64_t n);
+int gs_l1_forward(const float* pred, const float* target, int64_t n, void* workspace, size_t workspace_bytes,
+                  float* loss, void* stream);
+int gs_l1_backward(const float* pred, const float* target, int64_t n, const float* grad_loss, float* grad_pred,
+                   void* stream);
 
 /* Per-parameter Adam (mlx.optimizers.Adam as the trainer builds it,
  * trainer.py:128, update order of Adam.apply_single): per group

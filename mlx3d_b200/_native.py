@@ -121,6 +121,12 @@ _SIGS = {
     "gs_l1_ssim_backward": (
         c_int, [_P, _P, c_int, c_int, c_int, c_float, c_float, c_int, c_float, _P, c_size_t, c_float, _P, _P]
     ),
+    "gs_l1_ssim_backward_dev": (
+        c_int, [_P, _P, c_int, c_int, c_int, c_float, c_int, c_float, _P, c_size_t, _P, c_float, c_int, _P, _P]
+    ),
+    "gs_l1_workspace_bytes": (c_size_t, [c_int64]),
+    "gs_l1_forward": (c_int, [_P, _P, c_int64, _P, c_size_t, _P, _P]),
+    "gs_l1_backward": (c_int, [_P, _P, c_int64, _P, _P, _P]),
     "gs_adam_step": (c_int, [POINTER(GsAdamGroup), c_int, ctypes.c_double, ctypes.c_double, c_float, c_int, c_int64, _P]),
     "gs_rasterize_forward": (
         c_int,

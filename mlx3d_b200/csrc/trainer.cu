@@ -155,7 +155,9 @@ __global__ void k_loss_finish(const double* __restrict__ partials, int nblocks, 
 struct SsimBwdArgs {
   SsimArgs f;
   float lambda, scale;
-  float* grad;  // (H, W, C)
+  const float* scale_dev;  // if set, the scale is scale * scale_dev[0]
+  int accumulate;          // grad += instead of grad =
+  float* grad;             // (H, W, C)
 };
 
 __global__ void __launch_bounds__(kLossThreads) k_ssim_bwd(const SsimBwdArgs g) {
@@ -206,7 +208,57 @@ __global__ void __launch_bounds__(kLossThreads) k_ssim_bwd(const SsimBwdArgs g) 
   const float dssim = (f0 + 2.0f * p * f1 + t * f2) / numel;
   const float diff = p - t;
   const float sgn = diff > 0.0f ? 1.0f : (diff < 0.0f ? -1.0f : 0.0f);
-  g.grad[idx] = g.scale * ((1.0f - g.lambda) * sgn / numel - g.lambda * dssim);
+  const float scale = g.scale_dev ? g.scale * g.scale_dev[0] : g.scale;
+  const float v = scale * ((1.0f - g.lambda) * sgn / numel - g.lambda * dssim);
+  g.grad[idx] = g.accumulate ? g.grad[idx] + v : v;
+}
+
+// ---------------------------------------------------------------- L1 loss
+// mean |pred - target| over n values: per-block partial sums (float per
+// thread, double per block) and one finishing block, fixed order, so the
+// result does not depend on scheduling.
+constexpr int kL1Blocks = 148 * 4;
+constexpr int kL1Threads = 256;
+
+__global__ void __launch_bounds__(kL1Threads)
+k_l1_partial(const float* __restrict__ pred, const float* __restrict__ target, int64_t n,
+             double* __restrict__ partials) {
+  __shared__ double s[kL1Threads];
+  float acc = 0.0f;
+  for (int64_t i = (int64_t)blockIdx.x * kL1Threads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kL1Threads)
+    acc += fabsf(pred[i] - target[i]);
+  s[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = kL1Threads / 2; o > 0; o >>= 1) {
+    if ((int)threadIdx.x < o) s[threadIdx.x] += s[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) partials[blockIdx.x] = s[0];
+}
+
+__global__ void __launch_bounds__(kL1Threads)
+k_l1_finish(const double* __restrict__ partials, int nb, double n, float* __restrict__ loss) {
+  __shared__ double s[kL1Threads];
+  double acc = 0.0;
+  for (int b = threadIdx.x; b < nb; b += kL1Threads) acc += partials[b];
+  s[threadIdx.x] = acc;
+  __syncthreads();
+  for (int o = kL1Threads / 2; o > 0; o >>= 1) {
+    if ((int)threadIdx.x < o) s[threadIdx.x] += s[threadIdx.x + o];
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) loss[0] = (float)(s[0] / n);
+}
+
+// grad = g[0] * sign(pred - target) / n  (sign(0) = 0, the subgradient of
+// |x| that autodiff of abs uses).
+__global__ void k_l1_bwd(const float* __restrict__ pred, const float* __restrict__ target, int64_t n,
+                         const float* __restrict__ g, float* __restrict__ grad) {
+  const float scale = g[0] / (float)n;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const float d = pred[i] - target[i];
+    grad[i] = d > 0.0f ? scale : (d < 0.0f ? -scale : 0.0f);
+  }
 }
 
 // ------------------------------------------------------------------- Adam
@@ -297,12 +349,11 @@ int gs_l1_ssim_forward(const float* pred, const float* target, int height, int w
   return check_launch("k_ssim_fwd", 2);
 }
 
-int gs_l1_ssim_backward(const float* pred, const float* target, int height, int width, int channels,
-                        float lambda_dssim, float max_val, int window_size, float sigma,
-                        const void* workspace, size_t workspace_bytes, float grad_scale,
-                        float* grad_pred, void* stream) {
+static int l1_ssim_backward(const float* pred, const float* target, int height, int width, int channels,
+                            float lambda_dssim, int window_size, float sigma, const void* workspace,
+                            size_t workspace_bytes, float grad_scale, const float* grad_scale_dev,
+                            int accumulate, float* grad_pred, void* stream) {
   clear_error();
-  (void)max_val;  // the SSIM constants enter only through the forward's partial maps
   if (height <= 0 || width <= 0 || channels <= 0)
     return set_error(GS_ERR_INVALID_ARG, "image must be non-empty");
   if (!pred || !target || !grad_pred)
@@ -315,10 +366,60 @@ int gs_l1_ssim_backward(const float* pred, const float* target, int height, int 
   g.f.dmaps = reinterpret_cast<float*>(const_cast<void*>(workspace));
   g.lambda = lambda_dssim;
   g.scale = grad_scale;
+  g.scale_dev = grad_scale_dev;
+  g.accumulate = accumulate;
   g.grad = grad_pred;
   const dim3 grid((unsigned)ceil_div(width, kLT), (unsigned)ceil_div(height, kLT), (unsigned)channels);
   k_ssim_bwd<<<grid, kLossThreads, 0, as_stream(stream)>>>(g);
   return check_launch("k_ssim_bwd");
+}
+
+int gs_l1_ssim_backward(const float* pred, const float* target, int height, int width, int channels,
+                        float lambda_dssim, float max_val, int window_size, float sigma,
+                        const void* workspace, size_t workspace_bytes, float grad_scale,
+                        float* grad_pred, void* stream) {
+  (void)max_val;  // the SSIM constants enter only through the forward's partial maps
+  return l1_ssim_backward(pred, target, height, width, channels, lambda_dssim, window_size, sigma, workspace,
+                          workspace_bytes, grad_scale, nullptr, 0, grad_pred, stream);
+}
+
+int gs_l1_ssim_backward_dev(const float* pred, const float* target, int height, int width, int channels,
+                            float lambda_dssim, int window_size, float sigma, const void* workspace,
+                            size_t workspace_bytes, const float* grad_scale, float grad_sign, int accumulate,
+                            float* grad_pred, void* stream) {
+  if (!grad_scale) return set_error(GS_ERR_INVALID_ARG, "gs_l1_ssim_backward_dev: grad_scale is NULL");
+  return l1_ssim_backward(pred, target, height, width, channels, lambda_dssim, window_size, sigma, workspace,
+                          workspace_bytes, grad_sign, grad_scale, accumulate, grad_pred, stream);
+}
+
+size_t gs_l1_workspace_bytes(int64_t n) {
+  (void)n;
+  return sizeof(double) * kL1Blocks;
+}
+
+int gs_l1_forward(const float* pred, const float* target, int64_t n, void* workspace, size_t workspace_bytes,
+                  float* loss, void* stream) {
+  clear_error();
+  if (n <= 0) return set_error(GS_ERR_INVALID_ARG, "gs_l1_forward: n must be positive");
+  if (!pred || !target || !loss) return set_error(GS_ERR_INVALID_ARG, "gs_l1_forward: NULL pointer");
+  if (!workspace || workspace_bytes < gs_l1_workspace_bytes(n))
+    return set_error(GS_ERR_CAPACITY, "gs_l1_forward: workspace too small");
+  cudaStream_t s = as_stream(stream);
+  double* partials = reinterpret_cast<double*>(workspace);
+  k_l1_partial<<<kL1Blocks, kL1Threads, 0, s>>>(pred, target, n, partials);
+  k_l1_finish<<<1, kL1Threads, 0, s>>>(partials, kL1Blocks, (double)n, loss);
+  return check_launch("k_l1_partial", 2);
+}
+
+int gs_l1_backward(const float* pred, const float* target, int64_t n, const float* grad_loss, float* grad_pred,
+                   void* stream) {
+  clear_error();
+  if (n <= 0) return set_error(GS_ERR_INVALID_ARG, "gs_l1_backward: n must be positive");
+  if (!pred || !target || !grad_loss || !grad_pred)
+    return set_error(GS_ERR_INVALID_ARG, "gs_l1_backward: NULL pointer");
+  const unsigned grid = (unsigned)std::min<int64_t>(ceil_div(n, 256), 148 * 8);
+  k_l1_bwd<<<grid, 256, 0, as_stream(stream)>>>(pred, target, n, grad_loss, grad_pred);
+  return check_launch("k_l1_bwd");
 }
 
 int gs_adam_step(const gs_adam_group* groups, int n_groups, double beta1, double beta2, float eps,

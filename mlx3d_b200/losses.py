@@ -3,7 +3,8 @@
 ``ssim`` and ``l1_dssim_loss`` run on the fused sm_100a kernels behind
 ``gs_l1_ssim_forward`` / ``gs_l1_ssim_backward``: one forward kernel for the
 five windowed statistics, the SSIM and L1 sums, one backward kernel for the
-gradient of both terms.  ``psnr`` and ``l1_loss`` are one-line reductions.
+gradient of both terms.  ``l1_loss`` runs on ``gs_l1_forward`` /
+``gs_l1_backward``; ``psnr`` is a one-line reduction.
 """
 
 from __future__ import annotations
@@ -45,22 +46,46 @@ class _L1DSSIM(torch.autograd.Function):
         pred, target, ws = ctx.saved_tensors
         lam, max_val, window_size, sigma = ctx.args
         H, W, C = pred.shape
-        grad = torch.zeros_like(pred)
+        grad = torch.empty_like(pred)
         # d total = g_loss * d loss + g_l1 * d l1 + g_ssim * d ssim, each term linear in the
-        # kernel's (l1 weight, ssim weight) = (1 - lam, -lam): run it once per needed term.
+        # kernel's (l1 weight, ssim weight) = (1 - lam, -lam): one launch per needed term, the
+        # cotangent read on the device, the later terms accumulated into the first.
         terms = []
         if g_loss is not None:
-            terms.append((g_loss, lam))
+            terms.append((g_loss, 1.0, lam))
         if g_l1 is not None:
-            terms.append((g_l1, 0.0))
+            terms.append((g_l1, 1.0, 0.0))
         if g_ssim is not None:
-            terms.append((-g_ssim, 1.0))
-        for g, lam_k in terms:
-            part = torch.empty_like(pred)
-            nat.call("gs_l1_ssim_backward", nat.ptr(pred), nat.ptr(target), H, W, C, lam_k, max_val, window_size,
-                     sigma, nat.ptr(ws), ws.numel(), 1.0, nat.ptr(part), nat.stream())
-            grad += part * g
+            terms.append((g_ssim, -1.0, 1.0))
+        if not terms:
+            return torch.zeros_like(pred), None, None, None, None, None
+        for k, (g, sign, lam_k) in enumerate(terms):
+            g = g.detach().to(torch.float32).contiguous()
+            nat.call("gs_l1_ssim_backward_dev", nat.ptr(pred), nat.ptr(target), H, W, C, lam_k, window_size,
+                     sigma, nat.ptr(ws), ws.numel(), nat.ptr(g), sign, int(k > 0), nat.ptr(grad), nat.stream())
         return grad, None, None, None, None, None
+
+
+class _L1(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, pred, target):
+        lib = nat.load()
+        n = pred.numel()
+        ws = torch.empty((lib.gs_l1_workspace_bytes(n),), device=pred.device, dtype=torch.uint8)
+        loss = torch.empty((1,), device=pred.device, dtype=torch.float32)
+        nat.call("gs_l1_forward", nat.ptr(pred), nat.ptr(target), n, nat.ptr(ws), ws.numel(), nat.ptr(loss),
+                 nat.stream())
+        ctx.save_for_backward(pred, target)
+        return loss[0]
+
+    @staticmethod
+    def backward(ctx, g):
+        pred, target = ctx.saved_tensors
+        grad = torch.empty_like(pred)
+        g = g.detach().to(torch.float32).contiguous()
+        nat.call("gs_l1_backward", nat.ptr(pred), nat.ptr(target), pred.numel(), nat.ptr(g), nat.ptr(grad),
+                 nat.stream())
+        return grad, None
 
 
 def l1_dssim_loss(pred: torch.Tensor, target: torch.Tensor, lambda_dssim: float = 0.2, max_val: float = 1.0,
@@ -78,7 +103,13 @@ def ssim(pred: torch.Tensor, target: torch.Tensor, max_val: float = 1.0, window_
 
 
 def l1_loss(pred: torch.Tensor, target: torch.Tensor) -> torch.Tensor:
-    return (pred - target).abs().mean()
+    """mean |pred - target| on the fused sm_100a kernels (deterministic sum);
+    differentiable in pred."""
+    if pred.shape != target.shape:
+        raise ValueError("pred and target must have the same shape.")
+    pred = nat.require_cuda("pred", pred)
+    target = nat.require_cuda("target", target.detach())
+    return _L1.apply(pred.contiguous(), target.contiguous())
 
 
 def psnr(pred: torch.Tensor, target: torch.Tensor, max_val: float = 1.0) -> torch.Tensor:

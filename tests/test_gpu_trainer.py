@@ -35,6 +35,39 @@ def test_l1_dssim_loss_and_gradient_match_autodiff(shape):
     assert rel_l2(p.grad.cpu().numpy(), tp.grad.numpy()) < 1e-4
 
 
+@pytest.mark.parametrize("n", [1, 1000, 1080 * 1920 * 3])
+def test_l1_loss_and_gradient_match_torch(n):
+    rng = np.random.default_rng(n)
+    pred = rng.uniform(size=n).astype(np.float32)
+    target = rng.uniform(size=n).astype(np.float32)
+    target[: n // 7] = pred[: n // 7]  # ties: zero subgradient
+    p = torch.tensor(pred, device="cuda", requires_grad=True)
+    loss = losses.l1_loss(p, torch.tensor(target, device="cuda"))
+    (3.0 * loss).backward()
+    tp = torch.tensor(pred, dtype=torch.float64, requires_grad=True)
+    ref = (tp - torch.tensor(target, dtype=torch.float64)).abs().mean()
+    (3.0 * ref).backward()
+    assert abs(float(loss) - float(ref)) <= 1e-6 * max(1.0, abs(float(ref)))
+    np.testing.assert_allclose(p.grad.cpu().numpy(), tp.grad.numpy(), rtol=1e-6, atol=0)
+    # deterministic: same bits on a second evaluation
+    assert float(losses.l1_loss(p, torch.tensor(target, device="cuda"))) == float(loss)
+
+
+def test_l1_dssim_gradient_of_each_output_term():
+    rng = np.random.default_rng(5)
+    pred = rng.uniform(size=(40, 50, 3)).astype(np.float32)
+    target = rng.uniform(size=(40, 50, 3)).astype(np.float32)
+    p = torch.tensor(pred, device="cuda", requires_grad=True)
+    loss, l1, s = losses.l1_dssim_loss(p, torch.tensor(target, device="cuda"), 0.3)
+    (2.0 * loss + 0.5 * l1 - 1.5 * s).backward()
+    tp = torch.tensor(pred, dtype=torch.float64, requires_grad=True)
+    tt = torch.tensor(target, dtype=torch.float64)
+    rs = torch_ref.ssim(tp, tt)
+    rl1 = (tp - tt).abs().mean()
+    (2.0 * (0.7 * rl1 + 0.3 * (1.0 - rs)) + 0.5 * rl1 - 1.5 * rs).backward()
+    assert rel_l2(p.grad.cpu().numpy(), tp.grad.numpy()) < 1e-4
+
+
 def test_ssim_of_identical_images_is_one_and_gradient_flows():
     x = torch.rand(32, 48, 3, device="cuda", requires_grad=True)
     s = losses.ssim(x, x.detach())

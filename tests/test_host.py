@@ -45,6 +45,12 @@ def test_cpu_tensors_are_rejected():
     cam = Camera.look_at(eye=(0, 0, -3.0), width=32, height=32)
     with pytest.raises(ValueError, match="CUDA"):
         gs.project_gaussians(cam, torch.zeros(1, 3), torch.tensor([[1.0, 0, 0, 0]]), torch.ones(1, 3))
+    from mlx3d_b200 import losses
+
+    with pytest.raises(ValueError, match="CUDA"):
+        losses.l1_loss(torch.zeros(4), torch.zeros(4))
+    with pytest.raises(ValueError, match="shape"):
+        losses.l1_loss(torch.zeros(4), torch.zeros(5))
 
 
 def test_render_argument_validation():
