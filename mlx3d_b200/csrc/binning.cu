@@ -238,6 +238,7 @@ k_onesweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ val
   for (int i = threadIdx.x; i < nvalid; i += OS_THREADS) {
     const uint32_t key = s_keys[i];
     const uint32_t pos = s_base[(key >> shift) & 255u] + (uint32_t)i;
+    if ((int64_t)pos >= n) continue;  // only if the histograms disagree with the keys (inconsistent inputs)
     if (KEYS_OUT) keys_out[pos] = key;
     vals_out[pos] = s_vals[i];
   }
@@ -564,11 +565,12 @@ k_tile_hist(const uint32_t* __restrict__ tkeys, int64_t d, int passes, uint32_t*
 
 // [start, end) of every non-empty tile from the tile-sorted keys; empty
 // tiles keep the zero-initialised [0, 0) (tiles.py:175-180).
-__global__ void k_tile_ranges(const uint32_t* __restrict__ tkeys, int64_t d,
+__global__ void k_tile_ranges(const uint32_t* __restrict__ tkeys, int64_t d, int num_tiles,
                               int32_t* __restrict__ ranges) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= d) return;
   const uint32_t t = tkeys[i];
+  if (t >= (uint32_t)num_tiles) return;  // inconsistent inputs only
   if (i == 0 || tkeys[i - 1] != t) ranges[2 * (int64_t)t] = (int32_t)i;
   if (i == d - 1 || tkeys[i + 1] != t) ranges[2 * (int64_t)t + 1] = (int32_t)(i + 1);
 }
@@ -722,7 +724,7 @@ static int bin_end_impl(const float* means2d, const float* radii, const float* c
   uint32_t* kfinal = (passes % 2 == 1) ? tk1 : tk0;
   int e = radix_sort(tk0, tv0, tk1, tv1, d, passes, ws_d, M.st, kfinal, sorted_ids, s);
   if (e) return e;
-  k_tile_ranges<<<(unsigned)ceil_div(d, 256), 256, 0, s>>>(kfinal, d, tile_ranges);
+  k_tile_ranges<<<(unsigned)ceil_div(d, 256), 256, 0, s>>>(kfinal, d, num_tiles, tile_ranges);
   return check_launch("k_tile_ranges");
 }
 
