@@ -110,6 +110,32 @@ __device__ __forceinline__ int quad_mask(float2 m, float4 co, float pf, float4 b
   return mask;
 }
 
+// Staged per-Gaussian colours: one float4 per Gaussian when at most four
+// channels (one shared load per Gaussian), channel-major otherwise.
+template <int CMAX, int N>
+struct ColStage {
+  static constexpr bool kV4 = CMAX >= 1 && CMAX <= 4;
+  float4 v4[kV4 ? N : 1];
+  float s[kV4 ? 1 : (CMAX > 0 ? CMAX : 1)][kV4 ? 1 : N];
+  __device__ __forceinline__ void put(int ch, int j, float x) {
+    if (kV4)
+      (&v4[j].x)[ch] = x;
+    else
+      s[ch][j] = x;
+  }
+  __device__ __forceinline__ void get(int j, float* out) const {
+    if (kV4) {
+      const float4 q = v4[j];
+      const float t[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+      for (int ch = 0; ch < CMAX; ++ch) out[ch] = t[ch];
+    } else {
+#pragma unroll
+      for (int ch = 0; ch < CMAX; ++ch) out[ch] = s[ch][j];
+    }
+  }
+};
+
 // Forward compositor.  One CTA of 128 threads per tile (TilePixels layout);
 // each thread owns two pixels, so every staged Gaussian is read from shared
 // memory once per two pixels.  After staging a batch, each warp compacts
@@ -124,11 +150,10 @@ constexpr int kFwdBatch = 256;
 template <int CMAX, bool DEPTH>
 __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) {
   constexpr int NC = CMAX > 0 ? CMAX : 1;
-  __shared__ float2 s_xy[kFwdBatch];
+  __shared__ float4 s_xy[kFwdBatch];  // x, y, power floor
   __shared__ float4 s_co[kFwdBatch];  // conic a, b, c, opacity
-  __shared__ float s_pf[kFwdBatch];   // power floor
   __shared__ int s_qm[kFwdBatch];     // quad_mask
-  __shared__ float s_col[NC][kFwdBatch];
+  __shared__ ColStage<CMAX, kFwdBatch> s_col;
   __shared__ float s_z[DEPTH ? kFwdBatch : 1];
   __shared__ short s_list[kFwdThreads / 32][kFwdBatch];
 
@@ -171,15 +196,14 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
         const float4 co = make_float4(__ldg(a.conics + 3 * g), __ldg(a.conics + 3 * g + 1),
                                       __ldg(a.conics + 3 * g + 2), o);
         const float pf = power_floor(o);
-        s_xy[t] = m;
+        s_xy[t] = make_float4(m.x, m.y, pf, 0.0f);
         // -a/2 and -c/2: scaling by a power of two commutes with rounding, so
         // (-a/2 dx) dx + (-c/2 dy) dy == -0.5 ((a dx) dx + (c dy) dy) exactly
         s_co[t] = make_float4(-0.5f * co.x, co.y, -0.5f * co.z, co.w);
-        s_pf[t] = pf;
         s_qm[t] = quad_mask(m, co, pf, cull_box(m, co, pf), tile, a.tiles_x);
 #pragma unroll
         for (int ch = 0; ch < CMAX; ++ch)
-          if (ch < a.cc) s_col[ch][t] = __ldg(a.colors + (int64_t)g * a.c_total + a.c0 + ch);
+          if (ch < a.cc) s_col.put(ch, t, __ldg(a.colors + (int64_t)g * a.c_total + a.c0 + ch));
         if (DEPTH) s_z[t] = __ldg(a.depths + g);
       }
     }
@@ -199,9 +223,10 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
     for (int t = 0; t < cnt; ++t) {
       if (done[0] && done[1]) break;
       const int j = s_list[warp][t];
-      const float2 m = s_xy[j];
+      const float4 mq = s_xy[j];
+      const float2 m = make_float2(mq.x, mq.y);
       const float4 co = s_co[j];
-      const float pf = s_pf[j];
+      const float pf = mq.z;
       const float dx = gs_sub(m.x, pxf);
       const float adxdx = gs_mul(gs_mul(co.x, dx), dx);  // co.x = -a/2
       const float bdx = gs_mul(co.y, dx);
@@ -221,8 +246,10 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
           continue;
         }
         const float w = gs_mul(alpha, T[p]);
+        float cj[NC];
+        s_col.get(j, cj);
 #pragma unroll
-        for (int ch = 0; ch < CMAX; ++ch) acc[p][ch] = gs_add(acc[p][ch], gs_mul(s_col[ch][j], w));
+        for (int ch = 0; ch < CMAX; ++ch) acc[p][ch] = gs_add(acc[p][ch], gs_mul(cj[ch], w));
         if (DEPTH) dacc[p] = gs_add(dacc[p], gs_mul(s_z[j], w));
         T[p] = next_T;
         last[p] = b0 + j + 1;
@@ -313,11 +340,10 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
   constexpr int NV8 = (NV / 8) * 8;  // values reduced by warp_reduce8
   constexpr int BATCH = CMAX <= 4 ? 128 : 64;
   __shared__ int s_id[BATCH];
-  __shared__ float2 s_xy[BATCH];
+  __shared__ float4 s_xy[BATCH];
   __shared__ float4 s_co[BATCH];
-  __shared__ float s_pf[BATCH];
   __shared__ int s_qm[BATCH];
-  __shared__ float s_col[CMAX][BATCH];
+  __shared__ ColStage<CMAX, BATCH> s_col;
   // per-warp gradient totals; the +1 pitch puts the eight values a warp
   // stores for one Gaussian in eight different banks
   __shared__ float s_gw[kBwdWarps][NV][BATCH + 1];
@@ -388,14 +414,12 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         const float4 co = make_float4(__ldg(a.conics + 3 * gid), __ldg(a.conics + 3 * gid + 1),
                                       __ldg(a.conics + 3 * gid + 2), o);
         const float pf = power_floor(o);
-        s_xy[threadIdx.x] = m;
+        s_xy[threadIdx.x] = make_float4(m.x, m.y, pf, 0.0f);
         s_co[threadIdx.x] = make_float4(-0.5f * co.x, co.y, -0.5f * co.z, co.w);  // see the forward
-        s_pf[threadIdx.x] = pf;
         s_qm[threadIdx.x] = quad_mask(m, co, pf, cull_box(m, co, pf), tile, a.tiles_x);
 #pragma unroll
         for (int ch = 0; ch < CMAX; ++ch)
-          s_col[ch][threadIdx.x] =
-              ch < a.cc ? __ldg(a.colors + (int64_t)gid * a.c_total + a.c0 + ch) : 0.0f;
+          s_col.put(ch, threadIdx.x, ch < a.cc ? __ldg(a.colors + (int64_t)gid * a.c_total + a.c0 + ch) : 0.0f);
       }
     }
     for (int e = threadIdx.x; e < kBwdWarps * NV * (BATCH + 1); e += kBwdThreads) (&s_gw[0][0][0])[e] = 0.0f;
@@ -416,8 +440,9 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
       const int j = s_blist[warp][t];
 
       const float4 co = s_co[j];
-      const float2 m = s_xy[j];
-      const float pf = s_pf[j];
+      const float4 mq = s_xy[j];
+      const float2 m = make_float2(mq.x, mq.y);
+      const float pf = mq.z;
       float gv[NV];
 #pragma unroll
       for (int k = 0; k < NV; ++k) gv[k] = 0.0f;
@@ -445,9 +470,11 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         T[p] *= ra;
         const float aT = alpha * T[p];
         float cd = 0.0f;  // c . dL/dpix
+        float cj[CMAX];
+        s_col.get(j, cj);
 #pragma unroll
         for (int ch = 0; ch < CMAX; ++ch) {
-          cd += s_col[ch][j] * dpix[p][ch];
+          cd += cj[ch] * dpix[p][ch];
           gv[6 + ch] += aT * dpix[p][ch];
         }
         const float dL_dalpha = T[p] * cd - R[p] * ra;

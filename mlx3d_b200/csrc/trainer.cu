@@ -225,8 +225,22 @@ k_l1_partial(const float* __restrict__ pred, const float* __restrict__ target, i
              double* __restrict__ partials) {
   __shared__ double s[kL1Threads];
   float acc = 0.0f;
-  for (int64_t i = (int64_t)blockIdx.x * kL1Threads + threadIdx.x; i < n; i += (int64_t)gridDim.x * kL1Threads)
-    acc += fabsf(pred[i] - target[i]);
+  const int64_t stride = (int64_t)gridDim.x * kL1Threads;
+  const int64_t t0 = (int64_t)blockIdx.x * kL1Threads + threadIdx.x;
+  int64_t tail = 0;
+  if (((reinterpret_cast<uintptr_t>(pred) | reinterpret_cast<uintptr_t>(target)) & 15) == 0) {
+    // 16-byte vectors, four in flight per thread
+    const float4* p4 = reinterpret_cast<const float4*>(pred);
+    const float4* t4 = reinterpret_cast<const float4*>(target);
+    const int64_t nv = n >> 2;
+#pragma unroll 4
+    for (int64_t v = t0; v < nv; v += stride) {
+      const float4 a = __ldg(p4 + v), b = __ldg(t4 + v);
+      acc += (fabsf(a.x - b.x) + fabsf(a.y - b.y)) + (fabsf(a.z - b.z) + fabsf(a.w - b.w));
+    }
+    tail = nv << 2;
+  }
+  for (int64_t i = tail + t0; i < n; i += stride) acc += fabsf(pred[i] - target[i]);
   s[threadIdx.x] = acc;
   __syncthreads();
   for (int o = kL1Threads / 2; o > 0; o >>= 1) {
