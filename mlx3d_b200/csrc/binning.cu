@@ -281,68 +281,27 @@ k_depth_keys(const float* __restrict__ depths, const int32_t* __restrict__ count
   flush_hist(h, DEPTH_PASSES, ghist);
 }
 
-// Device-wide exclusive scan of counts[perm[i]] (int32), reduce-then-scan.
+// Device-wide exclusive scan of counts[perm[i]] (int32) in one kernel: a
+// block takes the next SC_TILE-element partition in launch order, scans it,
+// and finds the total of all earlier partitions by the same pointer-jumping
+// look-back as the radix passes (one word per partition: tag | reach | sum;
+// sums stay below 2^31 because D does).  The last partition writes D.
 constexpr int SC_THREADS = 256, SC_ITEMS = 16, SC_TILE = SC_THREADS * SC_ITEMS;
 
 __global__ void __launch_bounds__(SC_THREADS)
-k_scan_reduce(const int32_t* __restrict__ counts, const int32_t* __restrict__ perm, int64_t n,
-              unsigned long long* __restrict__ bsum) {
-  __shared__ unsigned long long ws[SC_THREADS / 32];
-  const int64_t base = (int64_t)blockIdx.x * SC_TILE;
-  unsigned long long s = 0;
-  for (int i = threadIdx.x; i < SC_TILE; i += SC_THREADS) {
-    const int64_t idx = base + i;
-    if (idx < n) s += (unsigned)counts[perm[idx]];
-  }
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = s;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned long long t = 0;
-    for (int w = 0; w < SC_THREADS / 32; ++w) t += ws[w];
-    bsum[blockIdx.x] = t;
-  }
-}
-
-// Single block: exclusive scan of the block sums; writes the grand total.
-constexpr int SB_THREADS = 1024;
-__global__ void __launch_bounds__(SB_THREADS)
-k_scan_bsums(unsigned long long* __restrict__ bsum, int nb, int64_t* __restrict__ total) {
-  __shared__ unsigned long long warp_sums[SB_THREADS / 32];
-  __shared__ unsigned long long carry;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  if (threadIdx.x == 0) carry = 0;
-  for (int start = 0; start < nb; start += SB_THREADS) {
-    const int i = start + threadIdx.x;
-    const unsigned long long x = i < nb ? bsum[i] : 0ull;
-    unsigned long long s = x;
-    for (int o = 1; o < 32; o <<= 1) {
-      const unsigned long long t = __shfl_up_sync(0xffffffffu, s, o);
-      if (lane >= o) s += t;
-    }
-    __syncthreads();
-    if (lane == 31) warp_sums[warp] = s;
-    __syncthreads();
-    unsigned long long pre = 0, tot = 0;
-    for (int w = 0; w < SB_THREADS / 32; ++w) {
-      const unsigned long long ws = warp_sums[w];
-      if (w < warp) pre += ws;
-      tot += ws;
-    }
-    const unsigned long long c = carry;
-    if (i < nb) bsum[i] = c + pre + s - x;
-    __syncthreads();
-    if (threadIdx.x == 0) carry = c + tot;
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) *total = (int64_t)carry;
-}
-
-__global__ void __launch_bounds__(SC_THREADS)
-k_scan_down(const int32_t* __restrict__ counts, const int32_t* __restrict__ perm, int64_t n,
-            const unsigned long long* __restrict__ bsum, uint32_t* __restrict__ offsets) {
+k_scan_chained(const int32_t* __restrict__ counts, const int32_t* __restrict__ perm, int64_t n, int nb,
+               unsigned long long* __restrict__ status, uint32_t* __restrict__ part_ctr,
+               uint32_t* __restrict__ offsets, int64_t* __restrict__ total_out) {
   __shared__ uint32_t warp_sums[SC_THREADS / 32];
-  const int64_t base = (int64_t)blockIdx.x * SC_TILE + (int64_t)threadIdx.x * SC_ITEMS;
+  __shared__ int s_part, s_fail;
+  __shared__ uint32_t s_excl;
+  if (threadIdx.x == 0) {
+    s_part = (int)atomicAdd(part_ctr, 1u);
+    s_fail = 0;
+  }
+  __syncthreads();
+  const int part = s_part;
+  const int64_t base = (int64_t)part * SC_TILE + (int64_t)threadIdx.x * SC_ITEMS;
   uint32_t c[SC_ITEMS];
   uint32_t local = 0;
 #pragma unroll
@@ -351,8 +310,38 @@ k_scan_down(const int32_t* __restrict__ counts, const int32_t* __restrict__ perm
     c[j] = idx < n ? (uint32_t)counts[perm[idx]] : 0u;
     local += c[j];
   }
-  uint32_t total;
-  uint32_t run = block_exclusive_scan(local, warp_sums, total) + (uint32_t)bsum[blockIdx.x];
+  uint32_t tot;
+  const uint32_t pre = block_exclusive_scan(local, warp_sums, tot);
+  if (threadIdx.x == 0) {
+    const unsigned long long tag = 1ull << 56;
+    unsigned long long* my = status + part;
+    st_relaxed_u64(my, tag | (1ull << 32) | tot);
+    uint32_t acc = tot;  // sum over partitions [cur + 1, part]
+    int64_t cur = part - 1;
+    int spins = 0;
+    while (cur >= 0) {
+      const unsigned long long w = ld_relaxed_u64(status + cur);
+      if ((w & (0xFFull << 56)) != tag) {
+        if (++spins > kLookbackSpins) {
+          s_fail = 1;
+          break;
+        }
+        __nanosleep(32);
+        continue;
+      }
+      acc += (uint32_t)w;
+      cur -= (int64_t)((w >> 32) & 0xFFFFFFull);
+      st_relaxed_u64(my, tag | ((unsigned long long)(part - cur) << 32) | acc);
+    }
+    s_excl = acc - tot;
+    if (part == nb - 1) *total_out = (int64_t)acc;
+  }
+  __syncthreads();
+  if (s_fail) {
+    if (threadIdx.x == 0) atomicAdd(&g_wait_failures, 1ull);
+    return;
+  }
+  uint32_t run = s_excl + pre;
 #pragma unroll
   for (int j = 0; j < SC_ITEMS; ++j) {
     const int64_t idx = base + j;
@@ -593,7 +582,7 @@ struct SortState {
 };
 
 struct NLayout {
-  size_t keys0, keys1, vals0, vals1, offsets, bsum, total;
+  size_t keys0, keys1, vals0, vals1, offsets, scan_status, scan_ctr, total;
   int nb_sc;
   SortState st;
   NLayout(int64_t n) : st(n, DEPTH_PASSES, 0) {
@@ -604,9 +593,11 @@ struct NLayout {
     vals0 = o; o += align256(4 * (size_t)n);
     vals1 = o; o += align256(4 * (size_t)n);
     offsets = o; o += align256(4 * (size_t)n);
-    bsum = o; o += align256(8 * (size_t)nb_sc);
     st = SortState(n, DEPTH_PASSES, o);
-    total = st.end;
+    o = st.end;  // the scan's look-back words follow, inside the same zeroed range
+    scan_status = o; o += 8 * (size_t)nb_sc;
+    scan_ctr = o; o += 256;
+    total = o;
   }
 };
 
@@ -629,8 +620,8 @@ static T* at(void* base, size_t off) {
   return reinterpret_cast<T*>(reinterpret_cast<char*>(base) + off);
 }
 
-static int zero_state(void* base, const SortState& st, cudaStream_t s) {
-  if (cudaMemsetAsync(at<char>(base, st.ghist), 0, st.end - st.ghist, s) != cudaSuccess)
+static int zero_range(void* base, size_t begin, size_t end, cudaStream_t s) {
+  if (cudaMemsetAsync(at<char>(base, begin), 0, end - begin, s) != cudaSuccess)
     return set_error(GS_ERR_CUDA, "cudaMemsetAsync failed");
   return GS_OK;
 }
@@ -707,7 +698,7 @@ static int bin_end_impl(const float* means2d, const float* radii, const float* c
   const int bits = tile_bits(num_tiles);
   const int passes = bits == 0 ? 1 : (bits + 7) / 8;
   if (passes > MAX_TILE_PASSES) return set_error(GS_ERR_CAPACITY, "too many tiles: %d", num_tiles);
-  if (int e = zero_state(ws_d, M.st, s)) return e;
+  if (int e = zero_range(ws_d, M.st.ghist, M.st.end, s)) return e;
   uint32_t* ghist = at<uint32_t>(ws_d, M.st.ghist);
   if (conics) {
     k_duplicate_refined<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(
@@ -781,7 +772,7 @@ int gs_bin_begin(const float* depths, const int32_t* tiles_touched, int64_t n, v
   uint32_t* k1 = at<uint32_t>(ws_n, L.keys1);
   int32_t* v0 = at<int32_t>(ws_n, L.vals0);
   int32_t* v1 = at<int32_t>(ws_n, L.vals1);
-  if (int e = zero_state(ws_n, L.st, s)) return e;
+  if (int e = zero_range(ws_n, L.st.ghist, L.total, s)) return e;
   k_depth_keys<<<(unsigned)std::min<int64_t>(ceil_div(n, 256), 148 * 8), 256, 0, s>>>(
       depths, tiles_touched, n, k0, v0, at<uint32_t>(ws_n, L.st.ghist));
   if (int e0 = check_launch("k_depth_keys")) return e0;
@@ -791,12 +782,11 @@ int gs_bin_begin(const float* depths, const int32_t* tiles_touched, int64_t n, v
   int e = radix_sort(k0, v0, k1, v1, n, DEPTH_PASSES, ws_n, L.st, nullptr, v0, s);
   if (e) return e;
   const int32_t* perm = v0;
-  unsigned long long* bsum = at<unsigned long long>(ws_n, L.bsum);
   uint32_t* offsets = at<uint32_t>(ws_n, L.offsets);
-  k_scan_reduce<<<L.nb_sc, SC_THREADS, 0, s>>>(tiles_touched, perm, n, bsum);
-  k_scan_bsums<<<1, SB_THREADS, 0, s>>>(bsum, L.nb_sc, d_total);
-  k_scan_down<<<L.nb_sc, SC_THREADS, 0, s>>>(tiles_touched, perm, n, bsum, offsets);
-  return check_launch("gs_bin_begin", 3);  // 3 scan kernels
+  k_scan_chained<<<L.nb_sc, SC_THREADS, 0, s>>>(tiles_touched, perm, n, L.nb_sc,
+                                               at<unsigned long long>(ws_n, L.scan_status),
+                                               at<uint32_t>(ws_n, L.scan_ctr), offsets, d_total);
+  return check_launch("k_scan_chained");
 }
 
 int gs_bin_end(const float* means2d, const float* radii, int64_t n, int64_t d, int width,
