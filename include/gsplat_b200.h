@@ -189,13 +189,15 @@ int gs_bin_end(const float* means2d, const float* radii, int64_t n, int64_t d, i
                int height, void* ws_n, size_t ws_n_bytes, void* ws_d, size_t ws_d_bytes,
                int32_t* sorted_ids, int32_t* tile_ranges, void* stream);
 
-/* The radix passes of gs_bin_begin / gs_bin_end are single kernels whose
- * blocks wait (bounded) for earlier blocks' digit counts.  A wait that ran
- * out leaves that block's keys unwritten and is counted on the device; this
- * reads the count for the current device (synchronous; reset != 0 clears
- * it).  Always 0 unless a GPU stalls for far longer than a pass takes.
- * No counterpart in the reference (its sort is mx.argsort). */
-int gs_bin_wait_failures(uint64_t* count, int reset);
+/* Bounded device-side waits: the radix passes and the offsets scan of
+ * gs_bin_begin / gs_bin_end (blocks wait for earlier blocks' counts) and the
+ * bulk (TMA) staging of gs_preprocess_forward / _backward (threads wait for
+ * the copy engine).  A wait that runs out leaves that block's output
+ * unwritten and is counted on the device; this reads the total for the
+ * current device (synchronous; reset != 0 clears it).  Always 0 unless a
+ * GPU stalls for far longer than a kernel takes.  No counterpart in the
+ * reference (its sort is mx.argsort; MLX stages nothing). */
+int gs_wait_failures(uint64_t* count, int reset);
 
 /* bin_gaussians with the reference's refine_tiles option (`conics` given,
  * tiles.py:91-164): a (Gaussian, tile) duplicate of the square bounding box

@@ -658,6 +658,15 @@ static int radix_sort(uint32_t* k0, int32_t* v0, uint32_t* k1, int32_t* v1, int6
   return GS_OK;
 }
 
+int binning_wait_failures(unsigned long long* out, int reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_wait_failures, sizeof(*out));
+  if (e == cudaSuccess && reset) {
+    const unsigned long long z = 0;
+    e = cudaMemcpyToSymbol(g_wait_failures, &z, sizeof(z));
+  }
+  return (int)e;
+}
+
 static int tile_bits(int num_tiles) {
   int b = 0;
   while ((1ll << b) < num_tiles) ++b;
@@ -724,19 +733,6 @@ extern "C" {
 
 size_t gs_bin_workspace_n_bytes(int64_t n) { return NLayout(n < 0 ? 0 : n).total; }
 
-int gs_bin_wait_failures(uint64_t* count, int reset) {
-  clear_error();
-  if (!count) return set_error(GS_ERR_INVALID_ARG, "count is NULL");
-  unsigned long long v = 0;
-  cudaError_t e = cudaMemcpyFromSymbol(&v, g_wait_failures, sizeof(v));
-  if (e == cudaSuccess && reset) {
-    const unsigned long long z = 0;
-    e = cudaMemcpyToSymbol(g_wait_failures, &z, sizeof(z));
-  }
-  if (e != cudaSuccess) return set_error(GS_ERR_CUDA, "gs_bin_wait_failures: %s", cudaGetErrorString(e));
-  *count = v;
-  return GS_OK;
-}
 
 int gs_bin_total(const int32_t* tiles_touched, int64_t n, int64_t* d_total, void* stream) {
   clear_error();

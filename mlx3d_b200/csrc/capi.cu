@@ -33,4 +33,16 @@ const char* gs_last_error(void) { return gs::g_last_error; }
 
 uint64_t gs_kernel_launch_count(void) { return gs::g_launches.load(std::memory_order_relaxed); }
 
+int gs_wait_failures(uint64_t* count, int reset) {
+  gs::clear_error();
+  if (!count) return gs::set_error(GS_ERR_INVALID_ARG, "count is NULL");
+  unsigned long long a = 0, b = 0;
+  int e = gs::binning_wait_failures(&a, reset);
+  if (e == 0) e = gs::preprocess_wait_failures(&b, reset);
+  if (e != 0)
+    return gs::set_error(GS_ERR_CUDA, "gs_wait_failures: %s", cudaGetErrorString((cudaError_t)e));
+  *count = a + b;
+  return GS_OK;
+}
+
 }  // extern "C"

@@ -31,6 +31,53 @@ inline bool aligned(const void* p, size_t a) {
   return (reinterpret_cast<uintptr_t>(p) % a) == 0;
 }
 
+// Device counters of bounded waits that ran out, one per translation unit
+// that waits (read synchronously, optionally reset; gs_wait_failures sums
+// them).  Return a cudaError_t.
+int binning_wait_failures(unsigned long long* out, int reset);
+int preprocess_wait_failures(unsigned long long* out, int reset);
+
+// ------------------------------------------------ bulk (TMA) copies
+// One-shot shared-memory mbarrier tracking bulk global->shared copies
+// (cp.async.bulk, the Blackwell/Hopper TMA engine without a tensor map;
+// never the cluster-multicast form).  Protocol: one thread calls
+// mbar_init, every thread passes a __syncthreads, one thread posts
+// mbar_arrive_expect_tx with the total byte count and issues bulk_g2s for
+// each piece, every thread calls mbar_wait(parity 0).  Addresses and sizes
+// of bulk copies are multiples of 16 bytes.
+__device__ __forceinline__ unsigned smem_addr(const void* p) {
+  return (unsigned)__cvta_generic_to_shared(p);
+}
+__device__ __forceinline__ void mbar_init(unsigned long long* bar, unsigned count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(unsigned long long* bar, unsigned bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.release.cta.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)),
+               "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes, unsigned long long* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(dst)),
+      "l"(src), "r"(bytes), "r"(smem_addr(bar))
+      : "memory");
+}
+// Bounded wait for phase `parity` of the barrier; false if it never completed.
+__device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity) {
+  for (int i = 0; i < (1 << 22); ++i) {
+    unsigned done;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+        : "=r"(done)
+        : "r"(smem_addr(bar)), "r"(parity)
+        : "memory");
+    if (done) return true;
+  }
+  return false;
+}
+
 // ------------------------------------------------ row staging through smem
 // A block of `rows` consecutive rows of `row_len` floats (row stride `stride`
 // floats) is copied into shared memory so that every global access is
@@ -42,6 +89,12 @@ inline bool aligned(const void* p, size_t a) {
 
 __device__ __forceinline__ bool rows_contiguous(const float* g, int64_t stride, int row_len) {
   return stride == row_len && (row_len & 1) && (reinterpret_cast<uintptr_t>(g) & 15) == 0;
+}
+
+// True when a row block can be fetched with one bulk copy: contiguous,
+// 16-byte aligned (rows_contiguous) and a whole number of 16-byte units.
+__device__ __forceinline__ bool rows_bulk(const float* g, int64_t stride, int row_len, int rows) {
+  return rows_contiguous(g, stride, row_len) && ((rows * row_len) & 3) == 0;
 }
 
 // Shared-memory pitch stage_rows uses for this row block.

@@ -212,6 +212,59 @@ struct PreFwdArgs {
 
 constexpr int kPreBlock = 128;
 
+__device__ unsigned long long g_wait_failures;
+
+// Staging of one block's parameter rows (means, scales, and the SH rows when
+// given).  Every row block that is contiguous, 16-byte aligned and a whole
+// number of 16-byte units is fetched with one bulk copy (cp.async.bulk,
+// issued by thread 0, completion on a shared-memory mbarrier); the others
+// with 16-byte cp.async or scalar loads by all threads (stage_rows).  The
+// decisions are block-uniform.  wait() completes both and synchronises the
+// block; false (for every thread) if the bulk copies did not complete within
+// the bounded wait, which is counted in g_wait_failures.
+struct StagePlan {
+  bool b_means, b_scales, b_dc, b_rest, want_dc, want_rest;
+  unsigned tx;
+  __device__ StagePlan(const float* g_means, const float* g_scales, const float* g_dc, int64_t dc_stride,
+                       const float* g_rest, int64_t rest_stride, int rest_len, int rows) {
+    want_dc = g_dc != nullptr;
+    want_rest = g_rest != nullptr && rest_len > 0;
+    b_means = rows_bulk(g_means, 3, 3, rows);
+    b_scales = rows_bulk(g_scales, 3, 3, rows);
+    b_dc = want_dc && rows_bulk(g_dc, dc_stride, 3, rows);
+    b_rest = want_rest && rows_bulk(g_rest, rest_stride, rest_len, rows);
+    tx = (b_means ? rows * 12u : 0u) + (b_scales ? rows * 12u : 0u) + (b_dc ? rows * 12u : 0u) +
+         (b_rest ? (unsigned)rows * (unsigned)rest_len * 4u : 0u);
+  }
+  __device__ void issue(unsigned long long* bar, float* s_means, const float* g_means, float* s_scales,
+                        const float* g_scales, float* s_dc, const float* g_dc, int64_t dc_stride, float* s_rest,
+                        const float* g_rest, int64_t rest_stride, int rest_len, int rows) const {
+    if (tx) {
+      if (threadIdx.x == 0) mbar_init(bar, 1);
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        mbar_arrive_expect_tx(bar, tx);
+        if (b_means) bulk_g2s(s_means, g_means, rows * 12u, bar);
+        if (b_scales) bulk_g2s(s_scales, g_scales, rows * 12u, bar);
+        if (b_dc) bulk_g2s(s_dc, g_dc, rows * 12u, bar);
+        if (b_rest) bulk_g2s(s_rest, g_rest, (unsigned)rows * (unsigned)rest_len * 4u, bar);
+      }
+    }
+    if (!b_means) stage_rows<kPreBlock>(s_means, g_means, 3, 3, rows);
+    if (!b_scales) stage_rows<kPreBlock>(s_scales, g_scales, 3, 3, rows);
+    if (want_dc && !b_dc) stage_rows<kPreBlock>(s_dc, g_dc, dc_stride, 3, rows);
+    if (want_rest && !b_rest) stage_rows<kPreBlock>(s_rest, g_rest, rest_stride, rest_len, rows);
+  }
+  __device__ bool wait(unsigned long long* bar) const {
+    cp_async_wait_all();
+    const bool ok = tx == 0 || mbar_wait(bar, 0);
+    if (__syncthreads_and(ok)) return true;
+    if (threadIdx.x == 0) atomicAdd(&g_wait_failures, 1ull);
+    return false;
+  }
+};
+
+
 __global__ void __launch_bounds__(kPreBlock) k_preprocess_fwd(const PreFwdArgs a) {
   extern __shared__ __align__(16) float smem[];
   const int64_t base = (int64_t)blockIdx.x * kPreBlock;
@@ -229,12 +282,12 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_fwd(const PreFwdArgs a
   float* s_scales = s_means + kPreBlock * 4;   // pitch <= 4
   float* s_dc = s_scales + kPreBlock * 4;      // pitch <= 4
   float* s_rest = s_dc + kPreBlock * 4;        // pitch <= rest_len | 1
-  stage_rows<kPreBlock>(s_means, g_means, 3, 3, rows);
-  stage_rows<kPreBlock>(s_scales, g_scales, 3, 3, rows);
-  if (a.fused && nb > 0) {
-    stage_rows<kPreBlock>(s_dc, g_dc, a.dc_stride, 3, rows);
-    if (rest_len > 0) stage_rows<kPreBlock>(s_rest, g_rest, a.rest_stride, rest_len, rows);
-  }
+  __shared__ unsigned long long s_bar;
+  const bool want_sh = a.fused && nb > 0;
+  const StagePlan plan(g_means, g_scales, want_sh ? g_dc : nullptr, a.dc_stride,
+                       want_sh && rest_len > 0 ? g_rest : nullptr, a.rest_stride, rest_len, rows);
+  plan.issue(&s_bar, s_means, g_means, s_scales, g_scales, s_dc, g_dc, a.dc_stride, s_rest, g_rest, a.rest_stride,
+             rest_len, rows);
   // This thread's own rows (quaternion, opacity) load while the staged
   // block lands.
   const int li = threadIdx.x;
@@ -245,8 +298,7 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_fwd(const PreFwdArgs a
     q = __ldg(reinterpret_cast<const float4*>(a.quats) + i);
     if (a.fused) o_raw = __ldg(a.opac + i);
   }
-  cp_async_wait_all();
-  __syncthreads();
+  if (!plan.wait(&s_bar)) return;
   if (li >= rows) return;
   float s0 = s_scales[li * sld + 0], s1 = s_scales[li * sld + 1], s2 = s_scales[li * sld + 2];
   if (a.flags & GS_ACT_EXP_SCALES) {
@@ -436,12 +488,10 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd(const PreBwdArgs g
   float* s_scales = s_means + kPreBlock * 4;
   float* s_dc = s_scales + kPreBlock * 4;      // sh_dc rows, then their gradients
   float* s_rest = s_dc + kPreBlock * 4;        // sh_rest rows, then their gradients
-  stage_rows<kPreBlock>(s_means, g_means, 3, 3, rows);
-  stage_rows<kPreBlock>(s_scales, g_scales, 3, 3, rows);
-  if (sh) {
-    stage_rows<kPreBlock>(s_dc, g_dc, a.dc_stride, 3, rows);
-    if (g_rest) stage_rows<kPreBlock>(s_rest, g_rest, a.rest_stride, rest_len, rows);
-  }
+  __shared__ unsigned long long s_bar;
+  const StagePlan plan(g_means, g_scales, sh ? g_dc : nullptr, a.dc_stride, g_rest, a.rest_stride, rest_len, rows);
+  plan.issue(&s_bar, s_means, g_means, s_scales, g_scales, s_dc, g_dc, a.dc_stride, s_rest, g_rest, a.rest_stride,
+             rest_len, rows);
   // This thread's own rows (quaternion, cotangents, opacity) load while
   // the staged block lands.
   const int li = threadIdx.x;
@@ -459,8 +509,7 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd(const PreBwdArgs g
       if (g.g_opac_out) goo = g.g_opac_out[i];
     }
   }
-  cp_async_wait_all();
-  __syncthreads();
+  if (!plan.wait(&s_bar)) return;
   if (li < rows) {
     const float r0 = s_scales[li * sld + 0], r1 = s_scales[li * sld + 1], r2 = s_scales[li * sld + 2];
     float s0 = r0, s1 = r1, s2 = r2;
@@ -595,6 +644,15 @@ static int check_cam(const gs_camera* cam) {
     return set_error(GS_ERR_INVALID_ARG, "camera size must be positive (got %dx%d)", cam->width,
                      cam->height);
   return GS_OK;
+}
+
+int preprocess_wait_failures(unsigned long long* out, int reset) {
+  cudaError_t e = cudaMemcpyFromSymbol(out, g_wait_failures, sizeof(*out));
+  if (e == cudaSuccess && reset) {
+    const unsigned long long z = 0;
+    e = cudaMemcpyToSymbol(g_wait_failures, &z, sizeof(z));
+  }
+  return (int)e;
 }
 
 }  // namespace gs

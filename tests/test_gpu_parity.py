@@ -337,7 +337,7 @@ def test_full_size_c2_properties():
     assert (radii[ids] > 0).all()
     # no radix-pass block gave up waiting for its predecessors
     cnt = ctypes.c_uint64(0)
-    nat.call("gs_bin_wait_failures", ctypes.byref(cnt), 1)
+    nat.call("gs_wait_failures", ctypes.byref(cnt), 1)
     assert cnt.value == 0
     # backward is linear in the output cotangent
     g = torch.randn_like(img)
