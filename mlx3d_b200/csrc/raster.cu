@@ -232,27 +232,34 @@ __global__ void __launch_bounds__(kFwdThreads) k_raster_fwd(const RasterArgs a) 
       const float bdx = gs_mul(co.y, dx);
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        if (done[p]) continue;
         const float dy = gs_sub(m.y, pyf[p]);
         const float power =
             gs_sub(gs_add(adxdx, gs_mul(gs_mul(co.z, dy), dy)), gs_mul(bdx, dy));
-        if (power > 0.0f || power < pf) continue;
-        // fminf == gs_minf here: neither operand is NaN
-        const float alpha = fminf(GS_ALPHA_MAX, gs_mul(co.w, gs_expf_nonpos(power)));
-        if (alpha < GS_ALPHA_MIN) continue;
+        // Predicated (no per-pixel branches): the exponential's argument is
+        // replaced by 0 where the pixel does not take the Gaussian, and
+        // every state update is a select, so composited values are the
+        // exact ones of the branchy form.  fminf == gs_minf here (no NaN).
+        bool take = !done[p] && power <= 0.0f && power >= pf;
+        const float alpha = fminf(GS_ALPHA_MAX, gs_mul(co.w, gs_expf_nonpos(take ? power : 0.0f)));
+        take = take && alpha >= GS_ALPHA_MIN;
         const float next_T = gs_mul(T[p], gs_sub(1.0f, alpha));
-        if (next_T < GS_T_MIN) {
-          done[p] = true;
-          continue;
-        }
+        const bool stop = take && next_T < GS_T_MIN;
+        done[p] = done[p] || stop;
+        take = take && !stop;
         const float w = gs_mul(alpha, T[p]);
         float cj[NC];
         s_col.get(j, cj);
 #pragma unroll
-        for (int ch = 0; ch < CMAX; ++ch) acc[p][ch] = gs_add(acc[p][ch], gs_mul(cj[ch], w));
-        if (DEPTH) dacc[p] = gs_add(dacc[p], gs_mul(s_z[j], w));
-        T[p] = next_T;
-        last[p] = b0 + j + 1;
+        for (int ch = 0; ch < CMAX; ++ch) {
+          const float na = gs_add(acc[p][ch], gs_mul(cj[ch], w));
+          acc[p][ch] = take ? na : acc[p][ch];
+        }
+        if (DEPTH) {
+          const float nd = gs_add(dacc[p], gs_mul(s_z[j], w));
+          dacc[p] = take ? nd : dacc[p];
+        }
+        T[p] = take ? next_T : T[p];
+        last[p] = take ? b0 + j + 1 : last[p];
       }
     }
   }
@@ -449,43 +456,43 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
       bool any = false;
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        if (!(b0 + j < last[p])) continue;
         const float dx = gs_sub(m.x, pxf), dy = gs_sub(m.y, pyf[p]);
         const float power = gs_sub(gs_add(gs_mul(gs_mul(co.x, dx), dx), gs_mul(gs_mul(co.z, dy), dy)),
                                    gs_mul(gs_mul(co.y, dx), dy));
-        if (power > 0.0f || power < pf) continue;
-        // The gradient needs e^power only to float accuracy, but the skip
+        // Predicated (no per-pixel branches): lanes that do not composite
+        // this Gaussian evaluate the same arithmetic and add zeros.  The
+        // gradient needs e^power only to float accuracy, but the skip
         // decision alpha < 1/255 must be the forward's: take the hardware
         // exponential (relative error ~1e-7) and redo it exactly only when
         // alpha lands within 1e-5 of the threshold.
-        float G = __expf(power);
+        bool take = b0 + j < last[p] && power <= 0.0f && power >= pf;
+        float G = __expf(take ? power : 0.0f);
         float alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, G));
-        if (fabsf(alpha - GS_ALPHA_MIN) < 1e-5f * GS_ALPHA_MIN) {
+        if (take && fabsf(alpha - GS_ALPHA_MIN) < 1e-5f * GS_ALPHA_MIN) {
           G = gs_expf(power);
           alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, G));
         }
-        if (alpha < GS_ALPHA_MIN) continue;
-        any = true;
+        take = take && alpha >= GS_ALPHA_MIN;
+        any = any || take;
         const float ra = __fdividef(1.0f, 1.0f - alpha);
-        T[p] *= ra;
-        const float aT = alpha * T[p];
-        float cd = 0.0f;  // c . dL/dpix
+        const float Tn = T[p] * ra;
+        const float aT = alpha * Tn;
+        float cd = 0.0f;
         float cj[CMAX];
         s_col.get(j, cj);
 #pragma unroll
-        for (int ch = 0; ch < CMAX; ++ch) {
-          cd += cj[ch] * dpix[p][ch];
-          gv[6 + ch] += aT * dpix[p][ch];
-        }
-        const float dL_dalpha = T[p] * cd - R[p] * ra;
-        R[p] += cd * aT;
+        for (int ch = 0; ch < CMAX; ++ch) cd += cj[ch] * dpix[p][ch];
+        const float dL_dalpha = Tn * cd - R[p] * ra;
+        const float gdl = take ? G * dL_dalpha : 0.0f;
+        const float aTm = take ? aT : 0.0f;
+#pragma unroll
+        for (int ch = 0; ch < CMAX; ++ch) gv[6 + ch] += aTm * dpix[p][ch];
         // d power / d(mean, conic) with u = G dL/dG (co.x = -a/2, co.z = -c/2):
         //   means2d: -u (a dx + b dy), -u (b dx + c dy)
         //   conic:   -u dx^2 / 2, -u dx dy, -u dy^2 / 2
         // are linear in the sums of u dx, u dy, u dx^2, u dx dy, u dy^2 over
         // the pixels (a, b, c fixed per Gaussian): those five sums are
         // accumulated and reduced, and the conic applied once per Gaussian.
-        const float gdl = G * dL_dalpha;
         const float u = co.w * gdl;
         const float ux = u * dx, uy = u * dy;
         gv[0] += ux;
@@ -494,6 +501,8 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         gv[3] += ux * dy;
         gv[4] += uy * dy;
         gv[5] += gdl;
+        T[p] = take ? Tn : T[p];
+        R[p] = take ? R[p] + cd * aT : R[p];
       }
       if (!__any_sync(0xffffffffu, any)) continue;
 #pragma unroll
