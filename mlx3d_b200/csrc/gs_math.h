@@ -132,8 +132,9 @@ GS_HD float gs_expf(float x) {
 
 // e^x for -87 <= x <= 0: the operations of gs_expf's fast path, with n =
 // rint(x log2e) taken by the round-to-nearest-even addition of 1.5 * 2^23
-// (exact for |x log2e| < 2^22; the sum's low mantissa bits hold n) instead
-// of rintf and a float-to-int conversion.  Bit-identical to gs_expf on that
+// (exact for |x log2e| < 2^22; the sum's low mantissa bits hold n, from
+// which 2^n is built with one integer multiply-add) instead of rintf and a
+// float-to-int conversion.  Bit-identical to gs_expf on that
 // interval (tests/test_oracle.py checks every float in it).
 GS_HD float gs_expf_nonpos(float x) {
   const float kLog2e = 1.44269502162933349609375f;
@@ -142,7 +143,7 @@ GS_HD float gs_expf_nonpos(float x) {
   const float kShift = 12582912.0f;  // 1.5 * 2^23
   const float s = gs_add(gs_mul(x, kLog2e), kShift);
   const float n = gs_sub(s, kShift);
-  const int k = (int)(gs_float_to_bits(s) - 0x4B400000u);
+  const uint32_t sb = gs_float_to_bits(s);  // low mantissa bits hold n
   float r = gs_fma(-n, kLn2Hi, x);
   r = gs_fma(-n, kLn2Lo, r);
   float p = 1.98412698412698412e-4f;
@@ -153,7 +154,9 @@ GS_HD float gs_expf_nonpos(float x) {
   p = gs_fma(p, r, 0.5f);
   p = gs_fma(p, r, 1.0f);
   p = gs_fma(p, r, 1.0f);
-  return gs_mul(p, gs_pow2i(k));
+  // 2^n as a float: its bits (n + 127) << 23 equal sb * 2^23 + 0x3F800000
+  // modulo 2^32 (sb = 0x4B400000 + n), one integer multiply-add.
+  return gs_mul(p, gs_bits_to_float(sb * 8388608u + 0x3F800000u));
 }
 
 // Logistic sigmoid 1 / (1 + e^-x) on top of gs_expf (model activations,
