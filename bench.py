@@ -211,7 +211,11 @@ def run_ours(args, world, rank, local):
         if overlap:
             reducer.launch()
         loss = l1_loss(out["image"], target_)
-        loss.backward()
+        if overlap:
+            with reducer.sink(pl):  # gradients land in the next flat all-reduce buffer
+                loss.backward()
+        else:
+            loss.backward()
         if overlap:
             while reducer.in_flight():
                 reducer.finish()

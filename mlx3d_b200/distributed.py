@@ -9,6 +9,8 @@ The reference has no multi-device code; this is the B200 build's addition.
 
 from __future__ import annotations
 
+import contextlib
+
 import torch
 import torch.distributed as dist
 
@@ -86,23 +88,58 @@ class GradientReducer:
     def in_flight(self) -> int:
         return len(self._pending)
 
-    def stage(self, params: dict[str, torch.Tensor] | list[torch.Tensor]) -> None:
-        tensors = list(params.values()) if isinstance(params, dict) else list(params)
+    def _slot_buffer(self, tensors: list[torch.Tensor]) -> torch.Tensor:
         total = sum(p.numel() for p in tensors)
+        buf = self._bufs[self._next]
+        if buf is None or buf.numel() != total or buf.device != tensors[0].device:
+            buf = self._bufs[self._next] = torch.empty(total, dtype=tensors[0].dtype, device=tensors[0].device)
+        return buf
+
+    @contextlib.contextmanager
+    def sink(self, params: dict[str, torch.Tensor] | list[torch.Tensor]):
+        """Within the block, the fused render's backward writes the gradients
+        of ``params`` straight into the buffer the next :meth:`stage` fills,
+        so staging them copies nothing (gradients that arrive elsewhere are
+        still copied)."""
+        from .splatting import render as _render
+
+        tensors = list(params.values()) if isinstance(params, dict) else list(params)
         if len(self._pending) >= 2:
             raise RuntimeError("GradientReducer: two reductions in flight; finish() one first")
-        i = self._next
+        buf = self._slot_buffer(tensors)
+        where, off = {}, 0
+        for p in tensors:
+            where[p.data_ptr()] = (off, p.shape, p.dtype)
+            off += p.numel()
+
+        def _sink(name, like):
+            # a fresh view per call: autograd adopts a returned gradient as
+            # .grad without a copy only when nothing else references it
+            w = where.get(like.data_ptr())
+            if w is None or w[1] != like.shape or w[2] != like.dtype:
+                return None
+            return buf[w[0]:w[0] + like.numel()].view(like.shape)
+
+        _render.set_grad_sink(_sink)
+        try:
+            yield
+        finally:
+            _render.set_grad_sink(None)
+
+    def stage(self, params: dict[str, torch.Tensor] | list[torch.Tensor]) -> None:
+        tensors = list(params.values()) if isinstance(params, dict) else list(params)
+        if len(self._pending) >= 2:
+            raise RuntimeError("GradientReducer: two reductions in flight; finish() one first")
+        buf = self._slot_buffer(tensors)
         self._next ^= 1
-        buf = self._bufs[i]
-        if buf is None or buf.numel() != total or buf.device != tensors[0].device:
-            buf = self._bufs[i] = torch.empty(total, dtype=tensors[0].dtype, device=tensors[0].device)
         off = 0
         for p in tensors:
             n = p.numel()
+            dst = buf[off:off + n]
             if p.grad is None:
-                buf[off:off + n].zero_()
-            else:
-                buf[off:off + n].copy_(p.grad.reshape(-1))
+                dst.zero_()
+            elif p.grad.data_ptr() != dst.data_ptr():  # not already written there by sink()
+                dst.copy_(p.grad.reshape(-1))
             off += n
         self._pending.append([None, buf])
 

@@ -131,10 +131,10 @@ class _Render(torch.autograd.Function):
             g_m2d += g_means2d_out
         if cfg.probe is not None:
             cfg.probe.copy_(g_m2d)
-        g_means = torch.empty_like(means)
-        g_quats = torch.empty_like(quats)
-        g_scales = torch.empty_like(scales)
-        g_opac = torch.empty_like(opacities)
+        g_means = _grad_like("means", means)
+        g_quats = _grad_like("quats", quats)
+        g_scales = _grad_like("scales", scales)
+        g_opac = _grad_like("opacities", opacities)
         use_sh = cfg.sh_mode != "colors"
         g_sh_a = g_sh_b = None
         g_dc = g_rest = None
@@ -142,13 +142,13 @@ class _Render(torch.autograd.Function):
             nb = num_sh_bases(cfg.sh_degree)
             if cfg.sh_mode == "full":
                 k = sh_a.shape[1]
-                g_sh_a = (torch.zeros_like if k > nb else torch.empty_like)(sh_a)
+                g_sh_a = _grad_like("sh_a", sh_a, zero=k > nb)
                 g_dc, g_rest = g_sh_a.data_ptr(), (g_sh_a.data_ptr() + 12) if k > 1 else None
             else:
-                g_sh_a = torch.empty_like(sh_a)
+                g_sh_a = _grad_like("sh_a", sh_a)
                 g_dc = g_sh_a.data_ptr()
                 if sh_b is not None:
-                    g_sh_b = (torch.zeros_like if sh_b.shape[1] + 1 > nb else torch.empty_like)(sh_b)
+                    g_sh_b = _grad_like("sh_b", sh_b, zero=sh_b.shape[1] + 1 > nb)
                     g_rest = nat.ptr(g_sh_b) if sh_b.numel() else None
         dc, dcs, rest, rests = _sh_layout(cfg, sh_a, sh_b)
         c = lambda t: None if t is None else t.contiguous()  # noqa: E731
@@ -161,6 +161,31 @@ class _Render(torch.autograd.Function):
         )
         g_colors = None if use_sh else g_col
         return g_means, g_quats, g_scales, g_opac, g_sh_a, g_sh_b, g_colors, None, None
+
+
+# Optional destination of the next backward's parameter gradients: a
+# callable (name, like) -> tensor shaped like `like` (or None for a fresh
+# one); names are "means", "quats", "scales", "opacities", "sh_a", "sh_b".
+# mlx3d_b200.distributed.GradientReducer installs one for the duration of a
+# backward so the gradients are written straight into its flat all-reduce
+# buffer.  A module global, not thread-local: autograd runs CUDA backward
+# functions on its own device thread.
+_grad_sink = None
+
+
+def set_grad_sink(fn) -> None:
+    global _grad_sink
+    _grad_sink = fn
+
+
+def _grad_like(name: str, like: torch.Tensor, zero: bool = False) -> torch.Tensor:
+    if _grad_sink is not None:
+        t = _grad_sink(name, like)
+        if t is not None:
+            if zero:
+                t.zero_()
+            return t
+    return torch.zeros_like(like) if zero else torch.empty_like(like)
 
 
 def _render_fused(

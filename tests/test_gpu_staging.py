@@ -38,3 +38,40 @@ def test_stager_rejects_pageable_host_memory_and_overfill():
     st.prefetch(h)
     with pytest.raises(RuntimeError):
         st.prefetch(h)
+
+
+def test_gradient_sink_writes_render_gradients_into_the_reducer_buffer():
+    from mlx3d_b200.distributed import GradientReducer
+    from mlx3d_b200.scenes import make_scene
+    from mlx3d_b200.splatting import GaussianModel
+
+    sc = make_scene(1, n=5000)
+    cam = sc.cameras[0]
+    target = sc.target(0)
+
+    def grads(use_sink):
+        params = sc.torch_params(requires_grad=True)
+        model = GaussianModel(params, sh_degree=3)
+        model.active_sh_degree = 3
+        red = GradientReducer()
+        out = model.render(cam)
+        loss = (out["image"] - target).abs().mean()
+        if use_sink:
+            with red.sink(params):
+                loss.backward()
+        else:
+            loss.backward()
+        red.stage(params)
+        flat = red.finish()
+        return params, flat
+
+    p1, f1 = grads(True)
+    p2, f2 = grads(False)
+    torch.cuda.synchronize()
+    # with the sink every gradient is a view of the reducer's flat buffer
+    lo, hi = f1.data_ptr(), f1.data_ptr() + f1.numel() * 4
+    assert all(lo <= p.grad.data_ptr() < hi for p in p1.values())
+    # (atomic accumulation order differs between two backward passes)
+    assert float((f1 - f2).norm() / f2.norm()) < 1e-5
+    for k in p1:
+        assert float((p1[k].grad - p2[k].grad).norm() / p2[k].grad.norm().clamp_min(1e-30)) < 1e-5, k
