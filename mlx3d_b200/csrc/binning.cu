@@ -13,7 +13,9 @@
 //   3. A stable LSD radix sort of the duplicates by tile id alone
 //      (ceil(log2(tiles)/8) passes, 1-2 for every configuration here).
 // Stable (tile, then depth order) == sort by tile * N + rank.
-//
+// Between 1 and 2, one chained-scan kernel turns the tiles-touched counts
+// (in depth order) into output offsets and D; 2 runs one warp per equal
+// chunk of the D outputs; 3 ends with the per-tile ranges.
 #include <algorithm>
 #include <utility>
 
@@ -21,16 +23,16 @@
 
 namespace gs {
 
-
 // ------------------------------------------------------------- radix passes
 // One kernel per 8-bit pass ("onesweep" structure):
 //   * the digit histograms of every pass come from the kernel that produces
 //     the keys (k_depth_keys, k_duplicate), so no pass re-reads its input to
 //     count;
 //   * a block takes the next partition of OS_TILE keys in launch order
-//     (atomic counter), ranks its keys stably by digit, publishes its
-//     per-digit counts and finds the counts of all earlier partitions by
-//     decoupled look-back over a per-partition status array;
+//     (atomic counter), ranks its keys stably by digit (warp multisplit by
+//     ballots), publishes its per-digit counts and finds the counts of all
+//     earlier partitions by a decoupled look-back with pointer jumping over
+//     a per-partition status array;
 //   * the keys are reordered by digit in shared memory and written out in
 //     digit runs, so consecutive threads store to consecutive addresses.
 // A partition only waits on partitions with smaller indices, which were
