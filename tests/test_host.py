@@ -7,7 +7,7 @@ import pytest
 import torch
 
 from mlx3d_b200 import splatting as gs
-from mlx3d_b200.cameras import Camera, fov_to_focal, look_at
+from mlx3d_b200.cameras import Camera, look_at
 from mlx3d_b200.scenes import CONFIGS, make_scene
 
 
