@@ -1,5 +1,10 @@
 """The trainable Gaussian scene (src/mlx3d/splatting/model.py).
 
+Adaptive density control (clone / split / prune, MCMC relocation, compact
+checkpoints, opacity reset; model.py:273-545) edits the Gaussian table with
+torch tensor operations on the parameters' own device: it is control of the
+set between optimisation steps, not part of the rendering path.
+
 Raw parameters live in ``self.params`` as torch leaf tensors:
 ``means`` (N, 3), ``scales`` (N, 3) log standard deviations, ``quats`` (N, 4)
 unnormalised wxyz, ``opacities`` (N,) logits, ``sh_dc`` (N, 1, 3) and
@@ -171,3 +176,170 @@ class GaussianModel:
     def one_up_sh_degree(self) -> None:
         if self.active_sh_degree < self.sh_degree:
             self.active_sh_degree += 1
+
+    # --------------------------------------------------- density control
+    def _set_params(self, new: dict[str, torch.Tensor]) -> None:
+        """Replace the tables by contiguous leaves, keeping requires_grad."""
+        out = {}
+        for k, v in new.items():
+            t = v.detach().contiguous()
+            old = self.params.get(k)
+            if old is not None and old.requires_grad:
+                t.requires_grad_(True)
+            out[k] = t
+        self.params = out
+
+    def copy(self) -> "GaussianModel":
+        """A detached copy of the Gaussian table (model.py:273-277)."""
+        out = GaussianModel({k: v.detach().clone() for k, v in self.params.items()}, self.sh_degree)
+        out.active_sh_degree = self.active_sh_degree
+        return out
+
+    def select(self, keep_idx) -> None:
+        """Keep only the rows ``keep_idx``, in that order (model.py:395-398)."""
+        idx = torch.as_tensor(keep_idx, dtype=torch.long, device=self.params["means"].device)
+        self._set_params({k: v.detach()[idx] for k, v in self.params.items()})
+
+    def append(self, new_params: dict[str, torch.Tensor]) -> None:
+        """Concatenate rows after the existing ones (model.py:400-404)."""
+        self._set_params({k: torch.cat([v.detach(), new_params[k].to(v)], dim=0) for k, v in self.params.items()})
+
+    def reset_opacities(self, max_opacity: float = 0.01) -> None:
+        """Clamp the opacity logits to logit(max_opacity) (model.py:533-538)."""
+        logit = math.log(max_opacity / (1.0 - max_opacity))
+        with torch.no_grad():
+            self.params["opacities"].clamp_(max=logit)
+
+    def compact(self, min_opacity: float = 0.0, max_gaussians: int | None = None,
+                target_sh_degree: int | None = None) -> "GaussianModel":
+        """A smaller checkpoint (model.py:279-336): rows with activated opacity
+        below ``min_opacity`` dropped (the most important row kept if none
+        survives), at most ``max_gaussians`` rows by importance
+        opacity * max(scale)^2, original order preserved, SH truncated to
+        ``target_sh_degree``; this model is not modified."""
+        if max_gaussians is not None and max_gaussians <= 0:
+            raise ValueError("max_gaussians must be positive when provided.")
+        if target_sh_degree is not None and not (0 <= target_sh_degree <= self.sh_degree):
+            raise ValueError("target_sh_degree must be between 0 and the model sh_degree.")
+        n = self.num_gaussians
+        if n == 0:
+            return self.copy()
+        with torch.no_grad():
+            opacity = self.opacities_act
+            max_scale = self.scales_act.max(dim=1).values
+            importance = opacity * max_scale * max_scale
+            keep = opacity >= float(min_opacity)
+            if not bool(keep.any()):
+                keep[int(torch.argmax(importance))] = True
+            keep_idx = torch.nonzero(keep).flatten()
+            if max_gaussians is not None and keep_idx.numel() > max_gaussians:
+                local = torch.topk(importance[keep_idx], max_gaussians).indices
+                keep_idx = keep_idx[local]
+            keep_idx = torch.sort(keep_idx).values
+            params = {k: v.detach()[keep_idx].clone() for k, v in self.params.items()}
+        sh_degree = self.sh_degree
+        if target_sh_degree is not None:
+            sh_degree = int(target_sh_degree)
+            k = num_sh_bases(sh_degree)
+            params["sh_rest"] = params["sh_rest"][:, : max(0, k - 1), :].contiguous()
+        out = GaussianModel(params, sh_degree=sh_degree)
+        out.active_sh_degree = min(self.active_sh_degree, sh_degree)
+        return out
+
+    def densify_and_prune(self, grad_accum: torch.Tensor, grad_count: torch.Tensor,
+                          grad_threshold: float = 0.0002, scene_extent: float = 1.0,
+                          percent_dense: float = 0.01, min_opacity: float = 0.005,
+                          return_optimizer_state: bool = False, generator: torch.Generator | None = None) -> dict:
+        """Adaptive density control of the 3DGS paper (model.py:406-480).
+
+        Average screen-space gradient = grad_accum / max(grad_count, 1); rows
+        above ``grad_threshold`` are cloned when their largest scale is at
+        most ``percent_dense * scene_extent``, otherwise split into two rows
+        drawn from the Gaussian (offsets R (s * N(0, 1)), log-scales reduced
+        by log 1.6).  Split sources, rows with opacity below ``min_opacity``
+        and rows larger than half the scene extent are pruned.  The kept rows
+        come first, then the clones, then the split pairs.  Returns the counts
+        (and, with ``return_optimizer_state``, the kept indices and the number
+        of appended rows, for resizing optimizer moments)."""
+        from .projection import quat_to_rotmat
+
+        dev = self.params["means"].device
+        with torch.no_grad():
+            avg_grad = grad_accum.to(dev) / torch.clamp(grad_count.to(dev), min=1.0)
+            scales = self.scales_act.detach()
+            max_scale = scales.max(dim=1).values
+            high_grad = avg_grad > grad_threshold
+            small = max_scale <= percent_dense * scene_extent
+            clone_idx = torch.nonzero(high_grad & small).flatten()
+            split_idx = torch.nonzero(high_grad & ~small).flatten()
+            p = {k: v.detach() for k, v in self.params.items()}
+            clones = {k: v[clone_idx] for k, v in p.items()}
+            splits = {}
+            if split_idx.numel() > 0:
+                R = quat_to_rotmat(p["quats"][split_idx])
+                s = scales[split_idx]
+                samples = torch.randn((split_idx.numel() * 2, 3), device=dev, dtype=s.dtype, generator=generator)
+                samples = samples * s.repeat_interleave(2, dim=0)
+                offsets = torch.einsum("nij,nj->ni", R.repeat_interleave(2, dim=0), samples)
+                splits = {k: v[split_idx].repeat_interleave(2, dim=0) for k, v in p.items()}
+                splits["means"] = splits["means"] + offsets
+                splits["scales"] = splits["scales"] - math.log(1.6)
+            opac = torch.sigmoid(torch.clamp(p["opacities"], -50.0, 50.0))
+            split_mask = high_grad & ~small
+            prune = (opac < min_opacity) | split_mask | (max_scale > 0.5 * scene_extent)
+            keep_idx = torch.nonzero(~prune).flatten()
+            new = {k: torch.cat([v[keep_idx], clones[k]] + ([splits[k]] if splits else []), dim=0)
+                   for k, v in p.items()}
+        self._set_params(new)
+        stats = {"cloned": int(clone_idx.numel()), "split": int(split_idx.numel()), "pruned": int(prune.sum())}
+        if return_optimizer_state:
+            stats["_keep_idx"] = keep_idx
+            stats["_new_count"] = int(clone_idx.numel() + 2 * split_idx.numel())
+        return stats
+
+    def relocate_mcmc(self, grad_accum: torch.Tensor, grad_count: torch.Tensor, relocate_frac: float = 0.02,
+                      min_opacity: float = 0.01, jitter_scale: float = 0.25,
+                      generator: torch.Generator | None = None) -> dict:
+        """Fixed-budget relocation (model.py:482-531): up to
+        ``relocate_frac * N`` underused rows (opacity below ``min_opacity`` or
+        never visible; the least opaque rows when none is underused) are
+        overwritten by copies of the highest-gradient other rows, with means
+        jittered by ``jitter_scale`` times the source scales, the opacity
+        reset to logit(0.05) and log-scales reduced by log 1.6.  N is kept."""
+        n = self.num_gaussians
+        max_relocate = int(max(0.0, min(relocate_frac, 1.0)) * n)
+        if max_relocate <= 0 or n <= 1:
+            return {"relocated": 0}
+        dev = self.params["means"].device
+        with torch.no_grad():
+            counts = grad_count.to(dev)
+            avg_grad = grad_accum.to(dev) / torch.clamp(counts, min=1.0)
+            opac = torch.sigmoid(self.params["opacities"].detach())
+            underused = (opac < min_opacity) | (counts <= 0)
+            n_under = int(underused.sum())
+            k = max_relocate if n_under == 0 else min(max_relocate, n_under)
+            k = min(k, n - 1)
+            if k == 0:
+                return {"relocated": 0}
+            target_score = torch.where(underused, 2.0 - opac, -opac)
+            dst = torch.topk(target_score, k).indices
+            source_score = avg_grad.clone()
+            source_score[dst] = -1e30
+            src = torch.topk(source_score, k).indices
+            source_scales = torch.exp(self.params["scales"].detach()[src])
+            new = {}
+            for name, arr in self.params.items():
+                arr = arr.detach()
+                values = arr[src].clone()
+                if name == "means" and jitter_scale > 0:
+                    noise = torch.randn(values.shape, device=dev, dtype=values.dtype, generator=generator)
+                    values = values + noise * source_scales * float(jitter_scale)
+                elif name == "opacities":
+                    values = torch.full_like(values, math.log(0.05 / 0.95))
+                elif name == "scales":
+                    values = values - math.log(1.6)
+                out = arr.clone()
+                out[dst] = values
+                new[name] = out
+        self._set_params(new)
+        return {"relocated": int(k), "_moved_idx": dst}

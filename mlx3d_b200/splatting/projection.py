@@ -140,12 +140,12 @@ def project_gaussians_ut(
     return {"means2d": means2d, "conics": conics, "depths": depths, "radii": radii, "compensation": comp}
 
 
-def quat_scale_to_cov3d(quats: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
-    """3D covariances ``R S S^T R^T`` (projection.py:17-21); a small host-side
-    utility (not on the rendering path), computed with torch ops."""
+def quat_to_rotmat(quats: torch.Tensor) -> torch.Tensor:
+    """Rotation matrices of (normalised) wxyz quaternions, (..., 3, 3); host
+    utility with torch ops (transforms.quaternion_to_matrix)."""
     q = quats / torch.linalg.norm(quats, dim=-1, keepdim=True)
     w, x, y, z = q.unbind(-1)
-    R = torch.stack(
+    return torch.stack(
         [
             1 - 2 * (y * y + z * z), 2 * (x * y - w * z), 2 * (x * z + w * y),
             2 * (x * y + w * z), 1 - 2 * (x * x + z * z), 2 * (y * z - w * x),
@@ -153,5 +153,11 @@ def quat_scale_to_cov3d(quats: torch.Tensor, scales: torch.Tensor) -> torch.Tens
         ],
         dim=-1,
     ).reshape(*quats.shape[:-1], 3, 3)
+
+
+def quat_scale_to_cov3d(quats: torch.Tensor, scales: torch.Tensor) -> torch.Tensor:
+    """3D covariances ``R S S^T R^T`` (projection.py:17-21); a small host-side
+    utility (not on the rendering path), computed with torch ops."""
+    R = quat_to_rotmat(quats)
     M = R * scales[..., None, :]
     return M @ M.transpose(-1, -2)

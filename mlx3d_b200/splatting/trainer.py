@@ -10,10 +10,12 @@ value at k - 1 and ``learning_rates()`` reports the rate of the last update
 (the behaviour pinned by the reference's test_trainer_position_lr_decays).
 
 Screen-space positional gradient norms are accumulated for densification
-(trainer.py:357-365), the opacity reset and SH-degree schedule run as in the
-reference; adaptive density control itself (clone / split / prune, MCMC
-relocation, 2DGS constraints — host-side control of the Gaussian set) is not
-part of this package: ``densify`` in the returned info is always ``None``.
+(trainer.py:357-365); every ``densify_every`` steps inside the window the
+model's adaptive density control runs (clone / split / prune, or MCMC
+relocation with ``method="mcmc"``, trainer.py:366-400) and the Adam moments
+follow the surviving rows (new rows start at zero).  The opacity reset and
+SH-degree schedule run as in the reference.  The 2DGS surfel method is not
+provided.
 """
 
 from __future__ import annotations
@@ -56,12 +58,18 @@ class TrainerConfig:
     densify_until: int = 15000
     densify_every: int = 100
     densify_grad_threshold: float = 0.0002
+    mcmc_relocate_frac: float = 0.02
+    mcmc_min_opacity: float = 0.01
+    mcmc_jitter_scale: float = 0.25
+    mcmc_noise_scale: float = 0.01
     opacity_reset_every: int = 3000
     sh_increase_every: int = 1000
     white_background: bool = False
     adam_betas: tuple = (0.9, 0.999)
     adam_eps: float = 1e-15
     adam_bias_correction: bool = False
+    max_gaussians: int | None = None
+    low_memory: bool = False  # releases torch's cached blocks after density events
 
 
 class GaussianTrainer:
@@ -70,9 +78,9 @@ class GaussianTrainer:
     def __init__(self, model: GaussianModel, config: TrainerConfig | None = None, scene_extent: float = 1.0):
         self.model = model
         self.config = config or TrainerConfig()
-        if self.config.method != "vanilla":
-            raise ValueError("TrainerConfig.method must be 'vanilla' in mlx3d_b200 ('mcmc' / '2dgs' control "
-                             "the Gaussian set and are not provided)")
+        if self.config.method not in {"vanilla", "mcmc"}:
+            raise ValueError("TrainerConfig.method must be 'vanilla' or 'mcmc' in mlx3d_b200 (the 2DGS surfel "
+                             "method is not provided)")
         if self.config.projection not in {"ewa", "ut"}:
             raise ValueError("TrainerConfig.projection must be 'ewa' or 'ut'")
         self.scene_extent = scene_extent
@@ -147,23 +155,70 @@ class GaussianTrainer:
         for k in _GROUPS:
             self.model.params[k].grad = None
 
+    # ----------------------------------------------------- density control
+    def _resize_moments(self, keep_idx: torch.Tensor, new_count: int) -> None:
+        """Adam moments of the surviving rows, zeros for appended ones
+        (trainer.py:139-159)."""
+        for k in _GROUPS:
+            for st in (self._m, self._v):
+                kept = st[k][keep_idx]
+                if new_count > 0:
+                    kept = torch.cat([kept, torch.zeros((new_count, *kept.shape[1:]), dtype=kept.dtype,
+                                                        device=kept.device)], dim=0)
+                st[k] = kept.contiguous()
+
+    def _zero_moment_rows(self, idx: torch.Tensor) -> None:
+        """Relocated rows restart their moments (trainer.py:161-179)."""
+        if idx is None or idx.numel() == 0:
+            return
+        for k in _GROUPS:
+            self._m[k][idx] = 0.0
+            self._v[k][idx] = 0.0
+
+    def _density_event(self) -> dict:
+        cfg = self.config
+        if cfg.method == "mcmc":
+            result = self.model.relocate_mcmc(self.grad_accum, self.grad_count, relocate_frac=cfg.mcmc_relocate_frac,
+                                              min_opacity=cfg.mcmc_min_opacity, jitter_scale=cfg.mcmc_jitter_scale)
+            self._zero_moment_rows(result.get("_moved_idx"))
+        else:
+            # At the cap, growth stops (infinite threshold) but pruning goes on.
+            at_cap = cfg.max_gaussians is not None and self.model.num_gaussians >= cfg.max_gaussians
+            threshold = float("inf") if at_cap else cfg.densify_grad_threshold
+            result = self.model.densify_and_prune(self.grad_accum, self.grad_count, grad_threshold=threshold,
+                                                  scene_extent=self.scene_extent, return_optimizer_state=True)
+            self._resize_moments(result["_keep_idx"], result["_new_count"])
+        self._reset_grad_accum()
+        if cfg.low_memory and torch.cuda.is_available():
+            torch.cuda.empty_cache()
+        return {k: v for k, v in result.items() if not str(k).startswith("_")}
+
+    def _mcmc_noise(self) -> None:
+        """SGLD-like position noise of the MCMC method (trainer.py:343-350)."""
+        cfg = self.config
+        if cfg.method != "mcmc" or cfg.mcmc_noise_scale <= 0:
+            return
+        sigma = cfg.mcmc_noise_scale * self.scene_extent * math.sqrt(max(self.learning_rates()["means"], 0.0))
+        if sigma > 0:
+            with torch.no_grad():
+                m = self.model.params["means"]
+                m.add_(torch.randn_like(m) * sigma)
+
     def _schedules_after_update(self) -> tuple[bool, bool]:
         cfg = self.config
         opacity_reset = sh_changed = False
         if self.step_count % cfg.opacity_reset_every == 0 and self.step_count <= cfg.densify_until:
-            with torch.no_grad():
-                logit = math.log(0.01 / 0.99)
-                self.model.params["opacities"].clamp_(max=logit)
+            self.model.reset_opacities(0.01)
             opacity_reset = True
         if self.step_count % cfg.sh_increase_every == 0:
             self.model.one_up_sh_degree()
             sh_changed = True
         return opacity_reset, sh_changed
 
-    def _info(self, loss: float, opacity_reset: bool, sh_changed: bool) -> dict:
+    def _info(self, loss: float, opacity_reset: bool, sh_changed: bool, densify: dict | None = None) -> dict:
         return {"loss": loss, "num_gaussians": self.model.num_gaussians, "step": self.step_count,
                 "active_sh_degree": self.model.active_sh_degree, "lr_means": self.learning_rates()["means"],
-                "method": self.config.method, "densify": None, "opacity_reset": opacity_reset,
+                "method": self.config.method, "densify": densify, "opacity_reset": opacity_reset,
                 "sh_degree_changed": sh_changed, "geometry": {}}
 
     # --------------------------------------------------------------- steps
@@ -174,14 +229,18 @@ class GaussianTrainer:
         probe = torch.zeros((self.model.num_gaussians, 2), device=target.device) if track else None
         loss, out = self._view_loss(camera, target, probe, 1.0)
         self._adam()
+        self._mcmc_noise()
+        densify = None
         if track:
             with torch.no_grad():
                 g = probe * torch.tensor([camera.width / 2.0, camera.height / 2.0], device=probe.device)
                 visible = (out["radii"] > 0).float()
                 self.grad_accum += g.norm(dim=-1) * visible
                 self.grad_count += visible
+            if self.step_count % cfg.densify_every == 0 and self.step_count > cfg.densify_from:
+                densify = self._density_event()
         opacity_reset, sh_changed = self._schedules_after_update()
-        return self._info(float(loss), opacity_reset, sh_changed)
+        return self._info(float(loss), opacity_reset, sh_changed, densify)
 
     def step_views(self, cameras: list[Camera], targets: list[torch.Tensor], total_views: int | None = None) -> dict:
         """One data-parallel step over a batch of views: this rank renders
@@ -197,6 +256,7 @@ class GaussianTrainer:
             loss_sum += loss
         allreduce_gradients({k: self.model.params[k] for k in _GROUPS})
         self._adam()
+        self._mcmc_noise()
         opacity_reset, sh_changed = self._schedules_after_update()
         info = self._info(float(loss_sum) / max(len(cameras), 1), opacity_reset, sh_changed)
         info["views"] = len(cameras)

@@ -155,3 +155,62 @@ def test_data_parallel_step_on_one_rank_equals_summed_views():
     t2._adam()
     for k in m1.params:
         assert rel_l2(m1.params[k].detach().cpu().numpy(), m2.params[k].detach().cpu().numpy()) < 1e-6, k
+
+
+def test_trainer_densification_runs():
+    """trainer.py:366-400 through GaussianTrainer.step (tests/test_splatting.py:705-717)."""
+    cam = Camera.look_at(eye=(0, 0, -3.0), at=(0, 0, 0), width=32, height=32)
+    target = torch.rand(32, 32, 3, device="cuda")
+    model = _model(40, 4)
+    trainer = gs.GaussianTrainer(model, gs.TrainerConfig(densify_from=2, densify_every=5,
+                                                         densify_grad_threshold=1e-9))
+    events = []
+    for _ in range(12):
+        info = trainer.step(cam, target)
+        if info["densify"] is not None:
+            events.append(info["densify"])
+    assert np.isfinite(info["loss"])
+    assert len(events) == 2 and events[0]["cloned"] + events[0]["split"] > 0
+    n = model.num_gaussians
+    assert info["num_gaussians"] == n
+    assert trainer.grad_accum.shape == (n,) and trainer.grad_count.shape == (n,)
+    for k in ("means", "scales", "quats", "opacities", "sh_dc", "sh_rest"):
+        assert trainer._m[k].shape == model.params[k].shape == trainer._v[k].shape
+        assert model.params[k].is_cuda and model.params[k].requires_grad
+
+
+def test_trainer_preserves_moments_after_densify_resize():
+    """trainer.py:139-159 (tests/test_splatting.py:720-751)."""
+    model = _model(8, 8)
+    trainer = gs.GaussianTrainer(model, gs.TrainerConfig(densify_from=10_000))
+    old_m = torch.arange(24, dtype=torch.float32, device="cuda").reshape(8, 3)
+    trainer._m["means"] = old_m.clone()
+    trainer._v["means"] = old_m + 100.0
+    keep = torch.tensor([1, 3, 6], device="cuda")
+    model.select(keep)
+    model.append({k: torch.zeros((2, *v.shape[1:]), device="cuda") for k, v in model.params.items()})
+    trainer._resize_moments(keep, 2)
+    zeros = torch.zeros(2, 3, device="cuda")
+    assert torch.equal(trainer._m["means"], torch.cat([old_m[keep], zeros]))
+    assert torch.equal(trainer._v["means"], torch.cat([old_m[keep] + 100.0, zeros]))
+    assert trainer._m["opacities"].shape == (5,)
+
+
+def test_trainer_mcmc_relocation_keeps_count_and_resets_moments():
+    """trainer.py:366-377 (tests/test_splatting.py:754-781)."""
+    cam = Camera.look_at(eye=(0, 0, -3.0), at=(0, 0, 0), width=32, height=32)
+    target = torch.rand(32, 32, 3, device="cuda")
+    model = _model(40, 13)
+    n0 = model.num_gaussians
+    cfg = gs.TrainerConfig(method="mcmc", densify_from=1, densify_every=2, densify_grad_threshold=1e-9,
+                           mcmc_relocate_frac=0.25, mcmc_min_opacity=0.2, mcmc_jitter_scale=0.0,
+                           mcmc_noise_scale=0.0)
+    trainer = gs.GaussianTrainer(model, cfg)
+    event = None
+    for _ in range(3):
+        info = trainer.step(cam, target)
+        if info["densify"] is not None:
+            event = info["densify"]
+    assert model.num_gaussians == n0
+    assert event is not None and event["relocated"] > 0
+    assert torch.isfinite(trainer._m["means"]).all()
