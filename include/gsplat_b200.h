@@ -199,6 +199,17 @@ int gs_bin_end(const float* means2d, const float* radii, int64_t n, int64_t d, i
  * reference (its sort is mx.argsort; MLX stages nothing). */
 int gs_wait_failures(uint64_t* count, int reset);
 
+/* Hard z-buffer mesh rasterizer over tile-binned triangles
+ * (src/mlx3d/renderer/rasterizer.py:29-79 and the call :150-162; the
+ * triangles are binned by bin_gaussians on their bounding circles).
+ * tri_xy (F, 3, 2) screen-space corners, tri_z (F, 3) camera-space depths,
+ * sorted_ids / tile_ranges from the binning; writes pix_to_face (H, W)
+ * (nearest triangle with depth > znear, -1 where none) and zbuf (H, W)
+ * (its interpolated depth, 0 where none). */
+int gs_mesh_rasterize(const float* tri_xy, const float* tri_z, int64_t n_faces, const int32_t* sorted_ids,
+                      const int32_t* tile_ranges, int width, int height, float znear, int32_t* pix_to_face,
+                      float* zbuf, void* stream);
+
 /* bin_gaussians with the reference's refine_tiles option (`conics` given,
  * tiles.py:91-164): a (Gaussian, tile) duplicate of the square bounding box
  * is kept only if the minimum of the conic form a dx^2 + 2 b dx dy + c dy^2

@@ -97,6 +97,7 @@ _SIGS = {
     "gs_bin_workspace_n_bytes": (c_size_t, [c_int64]),
     "gs_bin_workspace_d_bytes": (c_size_t, [c_int64]),
     "gs_wait_failures": (c_int, [_P, c_int]),
+    "gs_mesh_rasterize": (c_int, [_P, _P, c_int64, _P, _P, c_int, c_int, c_float, _P, _P, _P]),
     "gs_bin_total": (c_int, [_P, c_int64, _P, _P]),
     "gs_bin_begin": (c_int, [_P, _P, c_int64, _P, c_size_t, _P, _P]),
     "gs_bin_end": (c_int, [_P, _P, c_int64, c_int64, c_int, c_int, _P, c_size_t, _P, c_size_t, _P, _P, _P]),

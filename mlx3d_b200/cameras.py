@@ -113,6 +113,44 @@ class Camera:
     def world_to_camera(self, points: torch.Tensor) -> torch.Tensor:
         return points @ self.R.to(points).T + self.t.to(points)
 
+    def camera_to_world(self, points: torch.Tensor) -> torch.Tensor:
+        """Camera-frame points back to world coordinates (cameras.py:285-287)."""
+        return (points - self.t.to(points)) @ self.R.to(points)
+
+    def project_points(self, points: torch.Tensor, eps: float = 1e-8) -> tuple[torch.Tensor, torch.Tensor]:
+        """World points (..., 3) to pixel coordinates (..., 2) and camera-frame
+        depth (...,) (cameras.py:289-308): pinhole (or orthographic) with the
+        camera's lens distortion; differentiable torch operations (a host-side
+        utility, e.g. for the mesh rasterizer's vertices)."""
+        pc = self.world_to_camera(points)
+        z = pc[..., 2]
+        if self.orthographic:
+            return torch.stack([self.fx * pc[..., 0] + self.cx, self.fy * pc[..., 1] + self.cy], dim=-1), z
+        inv_z = 1.0 / torch.where(z.abs() < eps, torch.full_like(z, eps), z)
+        x, y = pc[..., 0] * inv_z, pc[..., 1] * inv_z
+        x, y = self._distort(x, y)
+        return torch.stack([self.fx * x + self.cx, self.fy * y + self.cy], dim=-1), z
+
+    def _distort(self, x: torch.Tensor, y: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Lens distortion of normalised coordinates (cameras.py:42-76)."""
+        c = self.distortion
+        if c is None:
+            return x, y
+        if self.fisheye:
+            k1, k2, k3, k4 = (list(c) + [0.0, 0.0, 0.0, 0.0])[:4]
+            r = torch.sqrt(x * x + y * y)
+            th = torch.atan(r)
+            th2 = th * th
+            thd = th * (1.0 + th2 * (k1 + th2 * (k2 + th2 * (k3 + th2 * k4))))
+            sc = thd / torch.clamp(r, min=1e-9)
+            return x * sc, y * sc
+        k1, k2, p1, p2 = c[0], c[1], c[2], c[3]
+        k3 = c[4] if len(c) > 4 else 0.0
+        r2 = x * x + y * y
+        radial = 1.0 + r2 * (k1 + r2 * (k2 + r2 * k3))
+        return (x * radial + 2.0 * p1 * x * y + p2 * (r2 + 2.0 * x * x),
+                y * radial + p1 * (r2 + 2.0 * y * y) + 2.0 * p2 * x * y)
+
     def lens_native(self) -> GsLens:
         """Lens model of this camera for the unscented projection."""
         lens = GsLens()

@@ -1,3 +1,4 @@
 from .protocols import Renderer, RenderOutput
+from .rasterizer import Fragments, interpolate_face_attributes, rasterize_meshes
 
-__all__ = ["RenderOutput", "Renderer"]
+__all__ = ["Fragments", "RenderOutput", "Renderer", "interpolate_face_attributes", "rasterize_meshes"]

@@ -547,6 +547,47 @@ void or_project_ut(const gs_camera* cam, const gs_lens* lens, const float* means
   }
 }
 
+// Hard z-buffer mesh rasterizer (src/mlx3d/renderer/rasterizer.py:29-79):
+// per pixel of each tile, the tile's binned triangles in order; barycentrics
+// by the reference's edge-function formula, skip |denom| < 1e-12, any
+// l < -1e-5 or z <= znear; keep the strictly nearest (first on ties).
+void or_mesh_rasterize(const float* tri_xy, const float* tri_z, const int32_t* ids, const int32_t* ranges,
+                       int width, int height, float znear, int32_t* pix_to_face, float* zbuf) {
+  const int tiles_x = (width + GS_TILE - 1) / GS_TILE, tiles_y = (height + GS_TILE - 1) / GS_TILE;
+#pragma omp parallel for schedule(dynamic, 4)
+  for (int tile = 0; tile < tiles_x * tiles_y; ++tile) {
+    const int tx = tile % tiles_x, ty = tile / tiles_x;
+    for (int ly = 0; ly < GS_TILE; ++ly)
+      for (int lx = 0; lx < GS_TILE; ++lx) {
+        const int px = tx * GS_TILE + lx, py = ty * GS_TILE + ly;
+        if (px >= width || py >= height) continue;
+        const float cx = (float)px + 0.5f, cy = (float)py + 0.5f;
+        int best_f = -1;
+        float best_z = 1e30f;
+        for (int k = ranges[2 * tile]; k < ranges[2 * tile + 1]; ++k) {
+          const int f = ids[k];
+          const float* t = tri_xy + (int64_t)f * 6;
+          const float ax = t[0], ay = t[1], bx = t[2], by = t[3], ccx = t[4], ccy = t[5];
+          const float denom = (by - ccy) * (ax - ccx) + (ccx - bx) * (ay - ccy);
+          if (fabsf(denom) < 1e-12f) continue;
+          const float l0 = ((by - ccy) * (cx - ccx) + (ccx - bx) * (cy - ccy)) / denom;
+          const float l1 = ((ccy - ay) * (cx - ccx) + (ax - ccx) * (cy - ccy)) / denom;
+          const float l2 = 1.0f - l0 - l1;
+          if (l0 < -1e-5f || l1 < -1e-5f || l2 < -1e-5f) continue;
+          const float* z3 = tri_z + (int64_t)f * 3;
+          const float z = l0 * z3[0] + l1 * z3[1] + l2 * z3[2];
+          if (z <= znear) continue;
+          if (z < best_z) {
+            best_z = z;
+            best_f = f;
+          }
+        }
+        pix_to_face[(int64_t)py * width + px] = best_f;
+        zbuf[(int64_t)py * width + px] = best_f >= 0 ? best_z : 0.0f;
+      }
+  }
+}
+
 // The shared exponential, exported so tests can check it against libm.
 float or_expf(float x) { return gs_expf(x); }
 

@@ -45,6 +45,7 @@ def load() -> ctypes.CDLL:
         lib.or_rasterize_bwd.argtypes = [P, P, P, c_int, P, c_int64, P, P, P, c_int, c_int, P, P, P, P, P, P, P, P,
                                          c_int]
         lib.or_project_ut.argtypes = [P, P, P, P, P, c_int64, c_float, c_int, P, P, P, P, P]
+        lib.or_mesh_rasterize.argtypes = [P, P, P, P, c_int, c_int, c_float, P, P]
         lib.or_expf.argtypes = [c_float]
         lib.or_expf.restype = c_float
         lib.or_expf_nonpos_mismatches.argtypes = []
@@ -144,6 +145,17 @@ def bin_gaussians(means2d, radii, depths, width, height, conics=None):
     ranges = np.empty((tx * ty, 2), np.int32)
     lib.or_bin_fill(_p(means2d), _p(radii), _p(depths), _p(conics), n, width, height, d, _p(ids), _p(ranges))
     return counts, ids, ranges, tx, ty
+
+
+def mesh_rasterize(tri_xy, tri_z, ids, ranges, width, height, znear):
+    """Hard z-buffer over binned triangles (renderer/rasterizer.py:29-79):
+    (pix_to_face (H, W) int32, zbuf (H, W))."""
+    tri_xy, tri_z, ids, ranges = _f32(tri_xy), _f32(tri_z), _i32(ids), _i32(ranges)
+    p2f = np.empty((height, width), np.int32)
+    zb = np.empty((height, width), np.float32)
+    load().or_mesh_rasterize(_p(tri_xy), _p(tri_z), _p(ids), _p(ranges), width, height, float(znear), _p(p2f),
+                             _p(zb))
+    return p2f, zb
 
 
 def rasterize_fwd(means2d, conics, colors, opac, ids, ranges, width, height, background=None, depths=None,

@@ -39,3 +39,33 @@ def max_rel(a, b) -> float:
 def t64(a, grad=False):
     t = torch.tensor(np.asarray(a), dtype=torch.float64)
     return t.requires_grad_(grad)
+
+
+def ico_sphere(level: int = 1, radius: float = 1.0):
+    """Icosphere (vertices (V, 3) float32, faces (F, 3) int32): the 12-vertex
+    icosahedron, each subdivision splitting every triangle into four with
+    edge midpoints pushed to the sphere."""
+    t = (1.0 + 5.0 ** 0.5) / 2.0
+    v = [(-1, t, 0), (1, t, 0), (-1, -t, 0), (1, -t, 0), (0, -1, t), (0, 1, t), (0, -1, -t), (0, 1, -t),
+         (t, 0, -1), (t, 0, 1), (-t, 0, -1), (-t, 0, 1)]
+    f = [(0, 11, 5), (0, 5, 1), (0, 1, 7), (0, 7, 10), (0, 10, 11), (1, 5, 9), (5, 11, 4), (11, 10, 2), (10, 7, 6),
+         (7, 1, 8), (3, 9, 4), (3, 4, 2), (3, 2, 6), (3, 6, 8), (3, 8, 9), (4, 9, 5), (2, 4, 11), (6, 2, 10),
+         (8, 6, 7), (9, 8, 1)]
+    verts = [np.array(p, dtype=np.float64) / np.linalg.norm(p) for p in v]
+    for _ in range(level):
+        mid = {}
+
+        def m(a, b):
+            key = (min(a, b), max(a, b))
+            if key not in mid:
+                p = verts[a] + verts[b]
+                verts.append(p / np.linalg.norm(p))
+                mid[key] = len(verts) - 1
+            return mid[key]
+
+        nf = []
+        for a, b, c in f:
+            ab, bc, ca = m(a, b), m(b, c), m(c, a)
+            nf += [(a, ab, ca), (b, bc, ab), (c, ca, bc), (ab, bc, ca)]
+        f = nf
+    return (np.array(verts) * radius).astype(np.float32), np.array(f, dtype=np.int32)
