@@ -108,3 +108,26 @@ def test_two_rank_pipelined_gradient_reducer():
             for step, s in enumerate(sums):
                 expect = torch.cat([torch.full((4,), float(20 * step + 1)), torch.full((6,), float(3 * step))])
                 torch.testing.assert_close(s, expect)
+
+
+def test_gradient_sink_hands_out_views_of_the_next_flat_buffer():
+    """GradientReducer.sink routes the fused render's gradient allocations
+    (render._grad_like) into the buffer the next stage() fills; stage() then
+    copies nothing for them (CPU tensors, world size 1)."""
+    from mlx3d_b200.distributed import GradientReducer
+    from mlx3d_b200.splatting import render as R
+
+    params = {"means": torch.randn(5, 3), "opacities": torch.randn(5)}
+    red = GradientReducer()
+    with red.sink(params):
+        gm = R._grad_like("means", params["means"])
+        go = R._grad_like("opacities", params["opacities"], zero=True)
+        other = R._grad_like("means", torch.randn(5, 3))  # not a parameter: a fresh tensor
+    assert R._grad_sink is None  # uninstalled on exit
+    gm.copy_(torch.full((5, 3), 2.0))
+    params["means"].grad, params["opacities"].grad = gm, go
+    red.stage(params)
+    flat = red.finish()
+    assert gm.data_ptr() == flat.data_ptr() and go.data_ptr() == flat.data_ptr() + 15 * 4
+    assert other.data_ptr() != flat.data_ptr()
+    torch.testing.assert_close(flat, torch.cat([torch.full((15,), 2.0), torch.zeros(5)]))
