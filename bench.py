@@ -1,14 +1,15 @@
 #!/usr/bin/env python
 """Benchmark of the splatting hot path on B200.
 
-Workload (the configuration the headline metric is quoted
-on): 1,000,000 Gaussians, SH degree 3, 1920x1080, fov 50, antialias on.  One
+Workload (benchmark config C2, the configuration the headline metric is
+quoted on): 1,000,000 Gaussians, SH degree 3, 1920x1080, fov 50, antialias on.  One
 step = GaussianModel.render(camera) forward (fused preprocess, binning,
 compositing) + L1 loss against a U(0,1) target + backward to every raw
 parameter (means, quats, log-scales, opacity logits, sh_dc, sh_rest).
 Under torchrun with N ranks each rank renders its own view of the same
 scene (weak scaling) and the per-Gaussian gradients (59 floats each) are
-summed over ranks with one NCCL all-reduce — the data-parallel training step.
+summed over ranks with one NCCL all-reduce, launched under the next view's
+backward (the step has no optimizer; --sync-allreduce waits every step).
 
 Prints one JSON line (rank 0).  `value` is whole-job milliseconds per frame:
 the max-over-ranks step time divided by the frames (views) the job rendered
@@ -147,7 +148,9 @@ def view_camera(scene, rank: int):
 
 
 # ---------------------------------------------------------------- our arm
-# Algorithmic bytes per unit of each entry point ("Roofline").
+# Algorithmic bytes per unit of each entry point: the bytes the entry point
+# must read and write once (inputs, outputs, and the passes its algorithm
+# needs), counted from the array sizes.
 def stage_bytes(stage: str, n: int, d: int, pixels: int, sh_rest_floats: int) -> float:
     sh = 4 * (3 + sh_rest_floats)
     if stage == "gs_preprocess_forward":
@@ -406,7 +409,7 @@ def run_ours(args, world, rank, local):
         line["cpu_baseline"] = cpu_baseline(scene, cam, cfg, steps=1)
         if rank == 0 and cam is scene.cameras[0]:
             # FP32 roofline of the two compositors (instruction-bound, not HBM-bound):
-            # algorithmic work per SURVEY 8(d) — 21 FLOP per pixel-Gaussian pair the
+            # algorithmic work of the reference's loops — 21 FLOP per pixel-Gaussian pair the
             # reference's forward loop evaluates, 45 FLOP per pair it composites
             # (backward) — counted exactly by the oracle on this frame, over the
             # kernels' live CUDA-event times.  Peak: nominal dense FP32,
