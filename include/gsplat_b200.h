@@ -32,6 +32,7 @@ extern "C" {
 #define GS_ERR_INVALID_ARG 1
 #define GS_ERR_CUDA 2
 #define GS_ERR_CAPACITY 3
+#define GS_ERR_TIMEOUT 4 /* a bounded device-side wait gave up (see gs_bin_status) */
 
 /* Activation flags for gs_preprocess_forward/backward
  * (src/mlx3d/splatting/model.py:116-122): scales given as log-scales,
@@ -199,6 +200,25 @@ int gs_bin_end(const float* means2d, const float* radii, int64_t n, int64_t d, i
  * reference (its sort is mx.argsort; MLX stages nothing). */
 int gs_wait_failures(uint64_t* count, int reset);
 
+/* Status of the last gs_bin_begin / gs_bin_end on this workspace_n
+ * (synchronises `stream`).  A binning look-back that gives up sets a bit in a
+ * status word inside workspace_n: 1 = depth sort, 2 = offsets scan, 4 = tile
+ * sort.  Every later binning kernel that depends on the failed stage does
+ * nothing, and every tile range stays the empty [0, 0), so a compositor
+ * launched on the outputs reads no Gaussian ids.  Returns GS_ERR_TIMEOUT when
+ * the word is non-zero (*status_out receives it).  gs_bin_status_offset(n)
+ * is the word's byte offset in workspace_n, for callers that copy it
+ * asynchronously instead.  Replaces nothing in the reference (mx.argsort,
+ * tiles.py:166-173, cannot time out). */
+int gs_bin_status(const void* ws_n, size_t ws_n_bytes, int64_t n, uint32_t* status_out, void* stream);
+size_t gs_bin_status_offset(int64_t n);
+
+/* Test hook: the number of polls a binning look-back makes before it gives
+ * up, on the current device (default 4194304).  0 makes every look-back that
+ * has to wait give up at once, which exercises the GS_ERR_TIMEOUT path
+ * without stalling anything.  No counterpart in the reference. */
+int gs_set_wait_limit(int polls);
+
 /* Hard z-buffer mesh rasterizer over tile-binned triangles
  * (src/mlx3d/renderer/rasterizer.py:29-79 and the call :150-162; the
  * triangles are binned by bin_gaussians on their bounding circles).
@@ -233,7 +253,12 @@ int gs_bin_end_refined(const float* means2d, const float* radii, const float* co
  * sorted_ids capacity below D (*d_out then holds the D needed).  Reads D back
  * to the host (one synchronisation of `stream`).  The first call on a device
  * looks up the array's device address: make it before any stream capture.
- * All calls share the array; calls that overlap on the GPU race. */
+ * The address is cached per device for the life of the process; after a
+ * cudaDeviceReset the cached address is stale, so do not call this entry
+ * point again in that process.  All calls share the array; calls that
+ * overlap on the GPU race.  A depth-sort or scan wait that gives up returns
+ * GS_ERR_TIMEOUT (found when D is read); a tile-sort wait that gives up
+ * leaves every tile range empty and is counted by gs_wait_failures. */
 #define GS_STATIC_BIN_MAX_N 131072
 #define GS_STATIC_BIN_MAX_D 1048576
 #define GS_STATIC_BIN_SCRATCH_BYTES (20u << 20)

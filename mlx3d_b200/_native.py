@@ -20,6 +20,7 @@ GS_OK = 0
 GS_ERR_INVALID_ARG = 1
 GS_ERR_CUDA = 2
 GS_ERR_CAPACITY = 3
+GS_ERR_TIMEOUT = 4
 
 GS_ACT_EXP_SCALES = 1
 GS_ACT_SIGMOID_OPACITY = 2
@@ -97,6 +98,9 @@ _SIGS = {
     "gs_bin_workspace_n_bytes": (c_size_t, [c_int64]),
     "gs_bin_workspace_d_bytes": (c_size_t, [c_int64]),
     "gs_wait_failures": (c_int, [_P, c_int]),
+    "gs_set_wait_limit": (c_int, [c_int]),
+    "gs_bin_status": (c_int, [_P, c_size_t, c_int64, ctypes.POINTER(ctypes.c_uint32), _P]),
+    "gs_bin_status_offset": (c_size_t, [c_int64]),
     "gs_mesh_rasterize": (c_int, [_P, _P, c_int64, _P, _P, c_int, c_int, c_float, _P, _P, _P]),
     "gs_bin_total": (c_int, [_P, c_int64, _P, _P]),
     "gs_bin_begin": (c_int, [_P, _P, c_int64, _P, c_size_t, _P, _P]),

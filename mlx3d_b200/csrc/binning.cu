@@ -37,8 +37,12 @@ namespace gs {
 //     digit runs, so consecutive threads store to consecutive addresses.
 // A partition only waits on partitions with smaller indices, which were
 // taken by blocks that are already running, so every wait ends; each wait is
-// still bounded (kLookbackSpins), after which the block records the failure
-// in g_wait_failures and writes nothing.
+// still bounded (g_wait_limit polls), after which the block counts the
+// failure in g_wait_failures, sets its stage's bit in the call's status word
+// (BinFail) and writes nothing.  Every later kernel that would index memory
+// with values the failed stage should have produced reads the status word
+// first and does nothing when a bit it depends on is set; the tile ranges
+// then stay all-empty, so a compositor launched afterwards reads no ids.
 //
 // Status words: pass + 1 (8 bits) | reach (24 bits) | count (32 bits): the
 // count of one digit over the `reach` partitions ending at this one.  One
@@ -53,7 +57,18 @@ constexpr int DEPTH_PASSES = 4;
 constexpr int MAX_TILE_PASSES = 4;
 constexpr int kLookbackSpins = 1 << 22;
 
+// Polls a look-back may make before it gives up (per device; set by
+// gs_set_wait_limit, for tests).  With 0, every look-back that has to read
+// an earlier partition's word gives up before its first read.
+__device__ int g_wait_limit = kLookbackSpins;
 __device__ unsigned long long g_wait_failures;
+
+// Bits of the per-call status word (in workspace_n, zeroed by gs_bin_begin).
+enum BinFail : uint32_t { kFailDepthSort = 1u, kFailScan = 2u, kFailTileSort = 4u };
+
+__device__ __forceinline__ uint32_t ld_status(const uint32_t* p) {
+  return *reinterpret_cast<const volatile uint32_t*>(p);
+}
 
 __device__ __forceinline__ void st_relaxed_u64(unsigned long long* p, unsigned long long v) {
   asm volatile("st.relaxed.gpu.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
@@ -125,7 +140,7 @@ __global__ void __launch_bounds__(OS_THREADS, 4)
 k_onesweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ vals_in,
            uint32_t* __restrict__ keys_out, int32_t* __restrict__ vals_out, int64_t n, int pass,
            const uint32_t* __restrict__ ghist, unsigned long long* __restrict__ status,
-           uint32_t* __restrict__ part_ctr) {
+           uint32_t* __restrict__ part_ctr, uint32_t* __restrict__ fail, uint32_t fail_bit) {
   __shared__ uint32_t wcnt[OS_WARPS][OS_RADIX];
   __shared__ uint32_t s_keys[OS_TILE];
   __shared__ int32_t s_vals[OS_TILE];
@@ -204,13 +219,15 @@ k_onesweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ val
   uint32_t acc = cnt_d;  // count over [cur + 1, part]
   int64_t cur = part - 1;
   int spins = 0;
+  const int limit = g_wait_limit;
   while (cur >= 0) {
+    if (spins >= limit) {
+      s_fail = 1;
+      break;
+    }
     const unsigned long long w = ld_relaxed_u64(status + cur * OS_RADIX + d);
     if ((w & (0xFFull << 56)) != tag) {  // not yet written in this pass
-      if (++spins > kLookbackSpins) {
-        s_fail = 1;
-        break;
-      }
+      ++spins;
       __nanosleep(32);
       continue;
     }
@@ -222,7 +239,10 @@ k_onesweep(const uint32_t* __restrict__ keys_in, const int32_t* __restrict__ val
   s_base[d] = gpre + excl - lstart;
   __syncthreads();
   if (s_fail) {
-    if (threadIdx.x == 0) atomicAdd(&g_wait_failures, 1ull);
+    if (threadIdx.x == 0) {
+      atomicAdd(&g_wait_failures, 1ull);
+      atomicOr(fail, fail_bit);
+    }
     return;
   }
 
@@ -293,10 +313,16 @@ constexpr int SC_THREADS = 256, SC_ITEMS = 16, SC_TILE = SC_THREADS * SC_ITEMS;
 __global__ void __launch_bounds__(SC_THREADS)
 k_scan_chained(const int32_t* __restrict__ counts, const int32_t* __restrict__ perm, int64_t n, int nb,
                unsigned long long* __restrict__ status, uint32_t* __restrict__ part_ctr,
-               uint32_t* __restrict__ offsets, int64_t* __restrict__ total_out) {
+               uint32_t* __restrict__ offsets, int64_t* __restrict__ total_out, uint32_t* __restrict__ fail) {
   __shared__ uint32_t warp_sums[SC_THREADS / 32];
   __shared__ int s_part, s_fail;
   __shared__ uint32_t s_excl;
+  // perm comes from the depth sort: if one of its look-backs gave up, perm
+  // may hold stale values and must not index counts.
+  if (ld_status(fail) & kFailDepthSort) {
+    if (blockIdx.x == 0 && threadIdx.x == 0) *total_out = 0;
+    return;
+  }
   if (threadIdx.x == 0) {
     s_part = (int)atomicAdd(part_ctr, 1u);
     s_fail = 0;
@@ -321,13 +347,15 @@ k_scan_chained(const int32_t* __restrict__ counts, const int32_t* __restrict__ p
     uint32_t acc = tot;  // sum over partitions [cur + 1, part]
     int64_t cur = part - 1;
     int spins = 0;
+    const int limit = g_wait_limit;
     while (cur >= 0) {
+      if (spins >= limit) {
+        s_fail = 1;
+        break;
+      }
       const unsigned long long w = ld_relaxed_u64(status + cur);
       if ((w & (0xFFull << 56)) != tag) {
-        if (++spins > kLookbackSpins) {
-          s_fail = 1;
-          break;
-        }
+        ++spins;
         __nanosleep(32);
         continue;
       }
@@ -336,11 +364,14 @@ k_scan_chained(const int32_t* __restrict__ counts, const int32_t* __restrict__ p
       st_relaxed_u64(my, tag | ((unsigned long long)(part - cur) << 32) | acc);
     }
     s_excl = acc - tot;
-    if (part == nb - 1) *total_out = (int64_t)acc;
+    if (part == nb - 1) *total_out = s_fail ? 0 : (int64_t)acc;
   }
   __syncthreads();
   if (s_fail) {
-    if (threadIdx.x == 0) atomicAdd(&g_wait_failures, 1ull);
+    if (threadIdx.x == 0) {
+      atomicAdd(&g_wait_failures, 1ull);
+      atomicOr(fail, (uint32_t)kFailScan);
+    }
     return;
   }
   uint32_t run = s_excl + pre;
@@ -435,8 +466,11 @@ __global__ void __launch_bounds__(256)
 k_duplicate(const float* __restrict__ means2d, const float* __restrict__ radii,
             const int32_t* __restrict__ perm, const uint32_t* __restrict__ offsets, int64_t n,
             int64_t d, int width, int height, int tiles_x, int tiles_y, uint32_t* __restrict__ tkeys,
-            int32_t* __restrict__ tvals, int passes, uint32_t* __restrict__ ghist) {
+            int32_t* __restrict__ tvals, int passes, uint32_t* __restrict__ ghist,
+            const uint32_t* __restrict__ fail) {
   __shared__ uint32_t h[MAX_TILE_PASSES][OS_RADIX];
+  // perm and offsets come from gs_bin_begin; skip if either stage gave up.
+  if (ld_status(fail) & (kFailDepthSort | kFailScan)) return;
   if (HIST) {
     for (int i = threadIdx.x; i < MAX_TILE_PASSES * OS_RADIX; i += blockDim.x) (&h[0][0])[i] = 0;
     __syncthreads();
@@ -520,9 +554,10 @@ __global__ void k_duplicate_refined(const float* __restrict__ means2d, const flo
                                     const float* __restrict__ conics, const int32_t* __restrict__ perm,
                                     const uint32_t* __restrict__ offsets, int64_t n, int64_t d, int width,
                                     int height, int tiles_x, int tiles_y, uint32_t* __restrict__ tkeys,
-                                    int32_t* __restrict__ tvals) {
+                                    int32_t* __restrict__ tvals, const uint32_t* __restrict__ fail) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= n) return;
+  if (ld_status(fail) & (kFailDepthSort | kFailScan)) return;
   const int32_t g = perm[i];
   const float2 m = reinterpret_cast<const float2*>(means2d)[g];
   int x0, y0, x1, y1;
@@ -557,9 +592,11 @@ k_tile_hist(const uint32_t* __restrict__ tkeys, int64_t d, int passes, uint32_t*
 // [start, end) of every non-empty tile from the tile-sorted keys; empty
 // tiles keep the zero-initialised [0, 0) (tiles.py:175-180).
 __global__ void k_tile_ranges(const uint32_t* __restrict__ tkeys, int64_t d, int num_tiles,
-                              int32_t* __restrict__ ranges) {
+                              int32_t* __restrict__ ranges, const uint32_t* __restrict__ fail) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= d) return;
+  // Any stage that gave up: every tile keeps the empty range [0, 0).
+  if (ld_status(fail) != 0u) return;
   const uint32_t t = tkeys[i];
   if (t >= (uint32_t)num_tiles) return;  // inconsistent inputs only
   if (i == 0 || tkeys[i - 1] != t) ranges[2 * (int64_t)t] = (int32_t)i;
@@ -584,7 +621,7 @@ struct SortState {
 };
 
 struct NLayout {
-  size_t keys0, keys1, vals0, vals1, offsets, scan_status, scan_ctr, total;
+  size_t keys0, keys1, vals0, vals1, offsets, scan_status, scan_ctr, fail, total;
   int nb_sc;
   SortState st;
   NLayout(int64_t n) : st(n, DEPTH_PASSES, 0) {
@@ -598,7 +635,8 @@ struct NLayout {
     st = SortState(n, DEPTH_PASSES, o);
     o = st.end;  // the scan's look-back words follow, inside the same zeroed range
     scan_status = o; o += 8 * (size_t)nb_sc;
-    scan_ctr = o; o += 256;
+    scan_ctr = o; o += 128;
+    fail = o; o += 128;  // BinFail status word of this call
     total = o;
   }
 };
@@ -634,7 +672,7 @@ static int zero_range(void* base, size_t begin, size_t end, cudaStream_t s) {
 // hold the input; k1/v1 are scratch.
 static int radix_sort(uint32_t* k0, int32_t* v0, uint32_t* k1, int32_t* v1, int64_t n, int passes,
                       void* base, const SortState& st, uint32_t* keys_final, int32_t* vals_final,
-                      cudaStream_t s) {
+                      uint32_t* fail, uint32_t fail_bit, cudaStream_t s) {
   const uint32_t* ghist = at<uint32_t>(base, st.ghist);
   uint32_t* ctr = at<uint32_t>(base, st.ctr);
   unsigned long long* status = at<unsigned long long>(base, st.status);
@@ -648,16 +686,20 @@ static int radix_sort(uint32_t* k0, int32_t* v0, uint32_t* k1, int32_t* v1, int6
     int32_t* vo = last ? vals_final : vout;
     if (ko)
       k_onesweep<true><<<st.nb, OS_THREADS, 0, s>>>(kin, vin, ko, vo, n, p, ghist + OS_RADIX * p, status,
-                                                     ctr + p);
+                                                     ctr + p, fail, fail_bit);
     else
       k_onesweep<false><<<st.nb, OS_THREADS, 0, s>>>(kin, vin, nullptr, vo, n, p, ghist + OS_RADIX * p,
-                                                      status, ctr + p);
+                                                      status, ctr + p, fail, fail_bit);
     if (int e = check_launch("k_onesweep")) return e;
     // The next pass reads what this one wrote.
     std::swap(kin, kout);
     std::swap(vin, vout);
   }
   return GS_OK;
+}
+
+int binning_set_wait_limit(int polls) {
+  return (int)cudaMemcpyToSymbol(g_wait_limit, &polls, sizeof(polls));
 }
 
 int binning_wait_failures(unsigned long long* out, int reset) {
@@ -702,6 +744,7 @@ static int bin_end_impl(const float* means2d, const float* radii, const float* c
   if (!means2d || !radii || !sorted_ids) return set_error(GS_ERR_INVALID_ARG, "gs_bin_end: NULL pointer");
   const int32_t* perm = at<int32_t>(ws_n, L.vals0);
   const uint32_t* offsets = at<uint32_t>(ws_n, L.offsets);
+  uint32_t* fail = at<uint32_t>(ws_n, L.fail);
   uint32_t* tk0 = at<uint32_t>(ws_d, M.keys0);
   uint32_t* tk1 = at<uint32_t>(ws_d, M.keys1);
   int32_t* tv0 = at<int32_t>(ws_d, M.vals0);
@@ -713,20 +756,20 @@ static int bin_end_impl(const float* means2d, const float* radii, const float* c
   uint32_t* ghist = at<uint32_t>(ws_d, M.st.ghist);
   if (conics) {
     k_duplicate_refined<<<(unsigned)ceil_div(n, 256), 256, 0, s>>>(
-        means2d, radii, conics, perm, offsets, n, d, width, height, tiles_x, tiles_y, tk0, tv0);
+        means2d, radii, conics, perm, offsets, n, d, width, height, tiles_x, tiles_y, tk0, tv0, fail);
     k_tile_hist<<<(unsigned)std::min<int64_t>(ceil_div(d, 256), 148 * 8), 256, 0, s>>>(tk0, d, passes, ghist);
     if (int e = check_launch("k_duplicate_refined", 2)) return e;
   } else {
     const unsigned grid = (unsigned)ceil_div(d, (int64_t)kDupChunk * 8);
     k_duplicate<true><<<grid, 256, 0, s>>>(means2d, radii, perm, offsets, n, d, width, height, tiles_x, tiles_y,
-                                           tk0, tv0, passes, ghist);
+                                           tk0, tv0, passes, ghist, fail);
     if (int e = check_launch("k_duplicate")) return e;
   }
   // Final keys land in whichever key buffer the last pass does not read.
   uint32_t* kfinal = (passes % 2 == 1) ? tk1 : tk0;
-  int e = radix_sort(tk0, tv0, tk1, tv1, d, passes, ws_d, M.st, kfinal, sorted_ids, s);
+  int e = radix_sort(tk0, tv0, tk1, tv1, d, passes, ws_d, M.st, kfinal, sorted_ids, fail, kFailTileSort, s);
   if (e) return e;
-  k_tile_ranges<<<(unsigned)ceil_div(d, 256), 256, 0, s>>>(kfinal, d, num_tiles, tile_ranges);
+  k_tile_ranges<<<(unsigned)ceil_div(d, 256), 256, 0, s>>>(kfinal, d, num_tiles, tile_ranges, fail);
   return check_launch("k_tile_ranges");
 }
 
@@ -777,13 +820,14 @@ int gs_bin_begin(const float* depths, const int32_t* tiles_touched, int64_t n, v
   // Pass p writes buffer (p + 1) % 2; with an even pass count the sorted
   // permutation lands in v0 (the last pass reads v1).  Keys are dropped.
   static_assert(DEPTH_PASSES % 2 == 0, "depth permutation buffer assumes an even pass count");
-  int e = radix_sort(k0, v0, k1, v1, n, DEPTH_PASSES, ws_n, L.st, nullptr, v0, s);
+  uint32_t* fail = at<uint32_t>(ws_n, L.fail);
+  int e = radix_sort(k0, v0, k1, v1, n, DEPTH_PASSES, ws_n, L.st, nullptr, v0, fail, kFailDepthSort, s);
   if (e) return e;
   const int32_t* perm = v0;
   uint32_t* offsets = at<uint32_t>(ws_n, L.offsets);
   k_scan_chained<<<L.nb_sc, SC_THREADS, 0, s>>>(tiles_touched, perm, n, L.nb_sc,
                                                at<unsigned long long>(ws_n, L.scan_status),
-                                               at<uint32_t>(ws_n, L.scan_ctr), offsets, d_total);
+                                               at<uint32_t>(ws_n, L.scan_ctr), offsets, d_total, fail);
   return check_launch("k_scan_chained");
 }
 
@@ -815,5 +859,34 @@ int gs_tile_counts_refined(const float* means2d, const float* radii, const float
       means2d, radii, conics, n, width, height, tx, ty, tiles_touched);
   return check_launch("k_tile_counts_refined");
 }
+
+int gs_bin_status(const void* ws_n, size_t ws_n_bytes, int64_t n, uint32_t* status_out, void* stream) {
+  clear_error();
+  if (!status_out) return set_error(GS_ERR_INVALID_ARG, "status_out is NULL");
+  if (n < 0 || n > INT32_MAX) return set_error(GS_ERR_INVALID_ARG, "n out of range: %lld", (long long)n);
+  const NLayout L(n);
+  if (n == 0) {  // gs_bin_begin / gs_bin_end launch nothing for n == 0
+    *status_out = 0;
+    return GS_OK;
+  }
+  if (!ws_n || ws_n_bytes < L.total)
+    return set_error(GS_ERR_CAPACITY, "workspace_n too small: %zu < %zu", ws_n_bytes, L.total);
+  cudaStream_t s = as_stream(stream);
+  uint32_t v = 0;
+  cudaError_t e = cudaMemcpyAsync(&v, at<char>(const_cast<void*>(ws_n), L.fail), sizeof(v),
+                                  cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return set_error(GS_ERR_CUDA, "gs_bin_status: %s", cudaGetErrorString(e));
+  *status_out = v;
+  if (v)
+    return set_error(GS_ERR_TIMEOUT,
+                     "a bounded device wait of the binning gave up (status 0x%x: %s%s%s); every tile range "
+                     "was left empty",
+                     v, (v & kFailDepthSort) ? "depth sort " : "", (v & kFailScan) ? "offsets scan " : "",
+                     (v & kFailTileSort) ? "tile sort" : "");
+  return GS_OK;
+}
+
+size_t gs_bin_status_offset(int64_t n) { return NLayout(n < 0 ? 0 : n).fail; }
 
 }  // extern "C"

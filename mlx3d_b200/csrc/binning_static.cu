@@ -22,7 +22,9 @@
 //
 // Set-up: the first call on a device looks up the device address of the
 // array (cudaGetSymbolAddress, with that device current) and caches it;
-// make that first call before any stream capture.  Each call reads the
+// make that first call before any stream capture.  The cache is not
+// invalidated: after a cudaDeviceReset the module is reloaded at another
+// address, so this entry point must not be called again in that process.  Each call reads the
 // duplicate count D back to the host (one stream synchronisation, as the
 // reference's bin_gaussians does with .item()).  Nothing here calls
 // cudaMalloc, cudaFree or an allocating library routine.
@@ -107,6 +109,10 @@ extern "C" int gs_bin_gaussians_static(const float* means2d, const float* radii,
   if (ce == cudaSuccess) ce = cudaStreamSynchronize(s);
   if (ce != cudaSuccess) return set_error(GS_ERR_CUDA, "reading D: %s", cudaGetErrorString(ce));
   *d_out = d;
+  uint32_t st = 0;  // the depth sort and scan have finished: their status is final
+  if (n > 0) {
+    if (int e = gs_bin_status(b + wsn_off, wsn_bytes, n, &st, stream)) return e;
+  }
   if (d > GS_STATIC_BIN_MAX_D)
     return set_error(GS_ERR_CAPACITY,
                      "gs_bin_gaussians_static: %lld duplicates exceed the static limit of %d",

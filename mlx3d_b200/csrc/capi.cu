@@ -33,6 +33,14 @@ const char* gs_last_error(void) { return gs::g_last_error; }
 
 uint64_t gs_kernel_launch_count(void) { return gs::g_launches.load(std::memory_order_relaxed); }
 
+int gs_set_wait_limit(int polls) {
+  gs::clear_error();
+  if (polls < 0) return gs::set_error(GS_ERR_INVALID_ARG, "polls must be >= 0");
+  int e = gs::binning_set_wait_limit(polls);
+  if (e != 0) return gs::set_error(GS_ERR_CUDA, "gs_set_wait_limit: %s", cudaGetErrorString((cudaError_t)e));
+  return GS_OK;
+}
+
 int gs_wait_failures(uint64_t* count, int reset) {
   gs::clear_error();
   if (!count) return gs::set_error(GS_ERR_INVALID_ARG, "count is NULL");

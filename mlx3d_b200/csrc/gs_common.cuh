@@ -35,6 +35,8 @@ inline bool aligned(const void* p, size_t a) {
 // that waits (read synchronously, optionally reset; gs_wait_failures sums
 // them).  Return a cudaError_t.
 int binning_wait_failures(unsigned long long* out, int reset);
+// Sets the poll limit of the binning look-backs on the current device.
+int binning_set_wait_limit(int polls);
 int preprocess_wait_failures(unsigned long long* out, int reset);
 
 // ------------------------------------------------ bulk (TMA) copies

@@ -10,11 +10,12 @@ The reference has no multi-device code; this is the B200 build's addition.
 from __future__ import annotations
 
 import contextlib
+import time
 
 import torch
 import torch.distributed as dist
 
-__all__ = ["shard_views", "allreduce_gradients", "GradientReducer", "world"]
+__all__ = ["shard_views", "allreduce_gradients", "GradientReducer", "PeerLost", "PeerMonitor", "world"]
 
 
 def world() -> tuple[int, int]:
@@ -141,6 +142,13 @@ class GradientReducer:
             elif p.grad.data_ptr() != dst.data_ptr():  # not already written there by sink()
                 dst.copy_(p.grad.reshape(-1))
             off += n
+        # Gradients that were written into the buffer by sink() alias it; the
+        # buffer is about to be reduced in place, so they are detached from
+        # the parameters (a later backward must not accumulate into, or read,
+        # memory under an in-flight all-reduce).
+        for p in tensors:
+            if p.grad is not None and buf.data_ptr() <= p.grad.data_ptr() < buf.data_ptr() + buf.numel() * buf.element_size():
+                p.grad = None
         self._pending.append([None, buf])
 
     def launch(self) -> None:
@@ -164,3 +172,72 @@ class GradientReducer:
         if work is not True:
             work.wait()  # the current stream waits for the collective
         return buf
+
+
+class PeerLost(RuntimeError):
+    """A rank stopped taking part: it left, exited or stopped answering."""
+
+    def __init__(self, rank: int, why: str):
+        super().__init__(f"rank {rank} {why}")
+        self.rank = rank
+
+
+class PeerMonitor:
+    """Host-side liveness check between steps, over the process group's
+    key-value store (no GPU work, no collective).
+
+    Every rank calls :meth:`beat` with the step number before it launches
+    the step's kernels and collectives: it publishes its heartbeat for that
+    step and waits, at most ``timeout`` seconds, for every other rank's.  A
+    rank that called :meth:`leave` makes the others raise :class:`PeerLost`
+    at once; one that exited or hangs makes them raise it after the
+    timeout.  Either way the survivors learn of it before their next launch
+    instead of blocking inside a collective whose peer is gone.  A rank may
+    only leave between steps, with none of its work in flight."""
+
+    def __init__(self, store=None, rank: int | None = None, world_size: int | None = None,
+                 timeout: float = 10.0, prefix: str = "mlx3d_b200/hb"):
+        if store is None:
+            from torch.distributed import distributed_c10d as c10d
+
+            store = c10d._get_default_store()
+        r, ws = world()
+        self.store = store
+        self.rank = r if rank is None else rank
+        self.world_size = ws if world_size is None else world_size
+        self.timeout = float(timeout)
+        self.prefix = prefix
+
+    def _key(self, kind: str, rank: int, step: int | None = None) -> str:
+        return f"{self.prefix}/{kind}/{rank}" + ("" if step is None else f"/{step}")
+
+    def leave(self) -> None:
+        """Announce that this rank takes part in no further step."""
+        self.store.set(self._key("left", self.rank), "1")
+
+    def beat(self, step: int) -> None:
+        """Publish this rank's heartbeat for ``step`` and wait for the others'."""
+        try:
+            self.store.set(self._key("beat", self.rank, step), "1")
+            waiting = [r for r in range(self.world_size) if r != self.rank]
+            deadline = time.monotonic() + self.timeout
+            delay = 1e-4
+            while waiting:
+                still = []
+                for r in waiting:
+                    if self.store.check([self._key("beat", r, step)]):
+                        continue
+                    if self.store.check([self._key("left", r)]):
+                        raise PeerLost(r, f"left before step {step}")
+                    still.append(r)
+                waiting = still
+                if not waiting:
+                    break
+                if time.monotonic() > deadline:
+                    raise PeerLost(waiting[0], f"sent no heartbeat for step {step} within {self.timeout:g} s")
+                time.sleep(delay)
+                delay = min(delay * 2, 0.01)
+        except PeerLost:
+            raise
+        except Exception as e:  # the store itself is gone (its host rank exited)
+            raise PeerLost(-1, f"unreachable: the key-value store failed ({type(e).__name__}: {e})") from e

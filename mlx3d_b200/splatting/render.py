@@ -264,6 +264,7 @@ def _render_fused(
     if depth is not None:
         out["depth"] = depth
     out["n_duplicates"] = cfg.duplicates
+    out["tiles_touched"] = counts
     return out
 
 

@@ -8,6 +8,7 @@ total D is read back to the host once per call to size the outputs.
 
 from __future__ import annotations
 
+import ctypes
 import threading
 
 import torch
@@ -16,9 +17,12 @@ from .. import _native as nat
 
 TILE_SIZE = 16
 
-__all__ = ["TILE_SIZE", "bin_gaussians", "bin_with_counts"]
+__all__ = ["TILE_SIZE", "bin_gaussians", "bin_with_counts", "check_pending_status"]
 
 _PINNED: dict = {}
+# (thread, device) -> (event, pinned status word) of the previous binning
+# whose status was copied to the host without waiting for it.
+_PENDING: dict = {}
 
 
 def _pinned_d() -> torch.Tensor:
@@ -31,6 +35,27 @@ def _pinned_d() -> torch.Tensor:
     return t
 
 
+def _raise_status(v: int) -> None:
+    raise RuntimeError(
+        f"binning: a bounded device wait gave up (status 0x{v:x}); every tile range was left empty, so the "
+        "frame rendered no Gaussians"
+    )
+
+
+def check_pending_status() -> None:
+    """Raise if a binning on this thread and device, whose status was copied
+    to the host without waiting, reported a device wait that gave up.  Status
+    copies that have not completed yet are left for a later check."""
+    key = (threading.get_ident(), torch.cuda.current_device())
+    pend = _PENDING.get(key)
+    if pend is None or not pend[0].query():
+        return
+    del _PENDING[key]
+    v = int(pend[1][0])
+    if v:
+        _raise_status(v)
+
+
 def bin_with_counts(
     means2d: torch.Tensor,
     radii: torch.Tensor,
@@ -39,10 +64,18 @@ def bin_with_counts(
     width: int,
     height: int,
     conics: torch.Tensor | None = None,
+    check: bool = False,
 ) -> tuple[torch.Tensor, torch.Tensor]:
     """Depth order, duplicates, tile sort and ranges, given per-Gaussian tile
     counts already computed (by the fused preprocess kernel, gs_tile_counts, or
-    gs_tile_counts_refined when ``conics`` is given for the tile refinement)."""
+    gs_tile_counts_refined when ``conics`` is given for the tile refinement).
+
+    The binning's look-backs are bounded device waits; one that gives up
+    leaves every tile range empty and sets a status word.  With ``check`` the
+    status is read synchronously and a failure raises ``RuntimeError`` here;
+    otherwise it is copied to the host asynchronously and raised by the next
+    binning call on this thread and device (whose own synchronisation on D
+    comes after it), or by ``check_pending_status``."""
     n = means2d.shape[0]
     dev = means2d.device
     tiles_x = (width + TILE_SIZE - 1) // TILE_SIZE
@@ -62,6 +95,7 @@ def bin_with_counts(
     nat.call("gs_bin_begin", nat.ptr(depths), nat.ptr(tiles_touched), n, nat.ptr(ws_n), ws_n.numel(),
              nat.ptr(d_total[1:]), s)
     ready.synchronize()
+    check_pending_status()
     d = int(d_host[0])
     ws_d = torch.empty((max(1, lib.gs_bin_workspace_d_bytes(d)),), device=dev, dtype=torch.uint8)
     sorted_ids = torch.empty((d,), device=dev, dtype=torch.int32)
@@ -77,6 +111,22 @@ def bin_with_counts(
             nat.ptr(ws_n), ws_n.numel(), nat.ptr(ws_d), ws_d.numel(), nat.ptr(sorted_ids) if d else None,
             nat.ptr(tile_ranges), s,
         )
+    if n == 0:
+        return sorted_ids, tile_ranges
+    off = lib.gs_bin_status_offset(n)
+    if check:
+        st = ctypes.c_uint32(0)
+        status = lib.gs_bin_status(nat.ptr(ws_n), ws_n.numel(), n, ctypes.byref(st), s)
+        if status == nat.GS_ERR_TIMEOUT:
+            _raise_status(st.value)
+        if status != nat.GS_OK:
+            raise RuntimeError(f"gs_bin_status failed (status {status}): {lib.gs_last_error().decode()}")
+    else:
+        flag = torch.empty((1,), dtype=torch.int32, pin_memory=True)
+        flag.copy_(ws_n[off:off + 4].view(torch.int32), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        _PENDING[(threading.get_ident(), torch.cuda.current_device())] = (ev, flag)
     return sorted_ids, tile_ranges
 
 
@@ -113,5 +163,5 @@ def bin_gaussians(
             raise ValueError("conics must have shape (N, 3).")
         nat.call("gs_tile_counts_refined", nat.ptr(means2d), nat.ptr(radii), nat.ptr(conics), n, width, height,
                  nat.ptr(counts), nat.stream())
-    sorted_ids, tile_ranges = bin_with_counts(means2d, radii, depths, counts, width, height, conics)
+    sorted_ids, tile_ranges = bin_with_counts(means2d, radii, depths, counts, width, height, conics, check=True)
     return sorted_ids, tile_ranges, tiles_x, tiles_y

@@ -242,11 +242,17 @@ class GaussianTrainer:
         opacity_reset, sh_changed = self._schedules_after_update()
         return self._info(float(loss), opacity_reset, sh_changed, densify)
 
-    def step_views(self, cameras: list[Camera], targets: list[torch.Tensor], total_views: int | None = None) -> dict:
+    def step_views(self, cameras: list[Camera], targets: list[torch.Tensor], total_views: int | None = None,
+                   monitor=None) -> dict:
         """One data-parallel step over a batch of views: this rank renders
         ``cameras`` (its shard), the loss is averaged over ``total_views``
         (all ranks' views), gradients are summed over ranks (NCCL all-reduce)
-        and one Adam update is applied on every rank."""
+        and one Adam update is applied on every rank.  With a
+        :class:`~mlx3d_b200.distributed.PeerMonitor`, the ranks exchange
+        heartbeats before anything is launched, so a rank that left makes
+        this raise ``PeerLost`` instead of blocking in the all-reduce."""
+        if monitor is not None:
+            monitor.beat(self.step_count)
         rank, ws = world()
         if total_views is None:
             total_views = len(cameras) * ws

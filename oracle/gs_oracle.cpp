@@ -15,7 +15,7 @@
 // only), so the oracle is pinned by the known-answer tests of the reference's
 // own test suite (tests/test_splatting.py:57-72, 114-195, 198-211) and by the
 // naive O(N*H*W) renderer of src/mlx3d/splatting/reference.py restated in
-// tests/oracle_torch.py; see tests/test_oracle.py.
+// oracle/torch_ref.py; see tests/test_oracle.py.
 #include <algorithm>
 #include <cmath>
 #include <cstdint>

@@ -131,3 +131,74 @@ def test_gradient_sink_hands_out_views_of_the_next_flat_buffer():
     assert gm.data_ptr() == flat.data_ptr() and go.data_ptr() == flat.data_ptr() + 15 * 4
     assert other.data_ptr() != flat.data_ptr()
     torch.testing.assert_close(flat, torch.cat([torch.full((15,), 2.0), torch.zeros(5)]))
+
+
+def _leaving_worker(rank, world_size, port, mode, results):
+    """Rank 1 takes part in step 0, then leaves (announced, or by exiting);
+    rank 0 must get PeerLost before step 1's collective, not hang in it."""
+    import time as _time
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world_size)
+    from mlx3d_b200.distributed import PeerLost, PeerMonitor
+
+    mon = PeerMonitor(timeout=1.0)
+    params = {"means": torch.zeros(3, requires_grad=True)}
+    params["means"].grad = torch.ones(3)
+    mon.beat(0)
+    allreduce_gradients(params)
+    if rank == 1:
+        if mode == "leave":
+            mon.leave()
+        results[rank] = "left"
+        # between steps, nothing in flight; wait until rank 0 reported (the
+        # store lives in rank 0's process), then exit without cleanup
+        deadline = _time.monotonic() + 60
+        while 0 not in results.keys() and _time.monotonic() < deadline:
+            _time.sleep(0.05)
+        os._exit(0)
+    t0 = _time.monotonic()
+    try:
+        mon.beat(1)
+        allreduce_gradients(params)
+        results[rank] = ("no error", float(params["means"].grad[0]))
+    except PeerLost as e:
+        results[rank] = ("PeerLost", e.rank, str(e), _time.monotonic() - t0)
+    os._exit(0)
+
+
+@pytest.mark.parametrize("mode", ["leave", "exit"])
+def test_survivor_learns_that_a_rank_left_between_steps(mode):
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_leaving_worker, args=(r, 2, port, mode, results)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+        assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+        r0 = results[0]
+    assert r0[0] == "PeerLost" and r0[1] == 1, r0
+    if mode == "leave":
+        assert "left before step 1" in r0[2] and r0[3] < 1.0
+    else:
+        assert "no heartbeat" in r0[2] and r0[3] < 10.0
+
+
+def test_peer_monitor_single_rank_and_store_failure():
+    from mlx3d_b200.distributed import PeerLost, PeerMonitor
+
+    class BrokenStore:
+        def set(self, k, v):
+            raise ConnectionError("closed")
+
+    store = dist.HashStore()
+    PeerMonitor(store=store, rank=0, world_size=1).beat(0)  # alone: returns at once
+    lone = PeerMonitor(store=store, rank=0, world_size=2, timeout=0.05)
+    with pytest.raises(PeerLost, match="no heartbeat"):
+        lone.beat(1)
+    with pytest.raises(PeerLost, match="unreachable"):
+        PeerMonitor(store=BrokenStore(), rank=0, world_size=2, timeout=0.1).beat(0)
