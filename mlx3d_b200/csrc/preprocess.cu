@@ -255,11 +255,22 @@ struct StagePlan {
     if (want_dc && !b_dc) stage_rows<kPreBlock>(s_dc, g_dc, dc_stride, 3, rows);
     if (want_rest && !b_rest) stage_rows<kPreBlock>(s_rest, g_rest, rest_stride, rest_len, rows);
   }
+  // Failure path: a CTA must not exit while a bulk copy still writes into
+  // its shared memory (what happens then is undefined).  So after the
+  // bounded wait gives up, thread 0 waits once more (bounded again) before
+  // the block leaves; if even that wait runs out, the block still leaves
+  // (there is no safe alternative that keeps the wait bounded) and the
+  // failure is counted, so the host can treat the launch's outputs as
+  // invalid.  The barrier is single-use and dies with the CTA.
   __device__ bool wait(unsigned long long* bar) const {
     cp_async_wait_all();
     const bool ok = tx == 0 || mbar_wait(bar, 0);
     if (__syncthreads_and(ok)) return true;
-    if (threadIdx.x == 0) atomicAdd(&g_wait_failures, 1ull);
+    if (threadIdx.x == 0) {
+      atomicAdd(&g_wait_failures, 1ull);
+      (void)mbar_wait(bar, 0);
+    }
+    __syncthreads();
     return false;
   }
 };

@@ -101,6 +101,7 @@ def test_render_forward_bit_exact(name):
     for k in ("means2d", "depths", "radii", "compensation", "image", "final_T", "n_contrib", "depth"):
         eq(npy(out[k]), ref[k], k)
     eq(npy(out["alpha"]), ref["alpha"], "alpha")
+    eq(npy(out["tiles_touched"]), ref["tiles_touched"], "tiles_touched")
 
 
 @pytest.mark.parametrize("name", ["random300", "c0", "c1"])

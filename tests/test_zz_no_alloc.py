@@ -45,7 +45,14 @@ def _static_bin(proj, width, height, capacity):
     return status, d.value, ids, ranges
 
 
+def _wait_failures(reset):
+    cnt = ctypes.c_uint64(0)
+    nat.call("gs_wait_failures", ctypes.byref(cnt), int(reset))
+    return cnt.value
+
+
 def test_static_binning_matches_workspace_binning_on_two_calls():
+    _wait_failures(reset=True)
     for index, n in ((1, 100_000), (0, 10_000)):
         cam, proj = _projected(index, n)
         ref_ids, ref_ranges, _, _ = gs.bin_gaussians(proj["means2d"], proj["radii"], proj["depths"], cam.width,
@@ -58,6 +65,19 @@ def test_static_binning_matches_workspace_binning_on_two_calls():
         np.testing.assert_array_equal(ids[:d].cpu().numpy(), ref_ids.cpu().numpy())
         np.testing.assert_array_equal(ranges.cpu().numpy(), ref_ranges.cpu().numpy())
         assert (ids[d:].cpu().numpy() == -7).all()  # nothing written past D
+    # no look-back of the sorts gave up (a give-up could leave partial output)
+    assert _wait_failures(reset=False) == 0
+
+
+def test_static_binning_of_no_gaussians():
+    tiles = 4 * 3
+    ranges = torch.full((tiles, 2), -7, dtype=torch.int32, device="cuda")
+    d = ctypes.c_int64(-1)
+    status = nat.load().gs_bin_gaussians_static(None, None, None, 0, 64, 48, 0, None, ranges.data_ptr(),
+                                                 ctypes.byref(d), torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    assert status == nat.GS_OK and d.value == 0
+    assert (ranges.cpu().numpy() == 0).all()
 
 
 def test_static_binning_rejects_sizes_beyond_its_limits():
@@ -66,6 +86,11 @@ def test_static_binning_rejects_sizes_beyond_its_limits():
     status, d, _, _ = _static_bin(proj, cam.width, cam.height, capacity=d_ref - 1)
     assert status == nat.GS_ERR_CAPACITY and d == d_ref
     assert b"needed" in nat.load().gs_last_error()
+    # more duplicates than the static limit: every Gaussian made 40x wider
+    wide = dict(proj, radii=proj["radii"] * 40.0)
+    status, d, _, _ = _static_bin(wide, cam.width, cam.height, capacity=1)
+    assert status == nat.GS_ERR_CAPACITY and d > 1048576, (status, d)
+    assert b"static limit" in nat.load().gs_last_error()
     lib = nat.load()
     big = 131072 + 1
     dd = ctypes.c_int64()
