@@ -450,22 +450,35 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
       const float4 mq = s_xy[j];
       const float2 m = make_float2(mq.x, mq.y);
       const float pf = mq.z;
+      // Cheap test first: power and the opacity floor decide every pair
+      // except those in the floor's 1e-3 margin, so a step in which no lane
+      // passes it (about a fifth of them at C2) skips the rest.
+      const float dx = gs_sub(m.x, pxf);
+      float dyv[2], pw[2];
+      bool pre[2];
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        dyv[p] = gs_sub(m.y, pyf[p]);
+        pw[p] = gs_sub(gs_add(gs_mul(gs_mul(co.x, dx), dx), gs_mul(gs_mul(co.z, dyv[p]), dyv[p])),
+                       gs_mul(gs_mul(co.y, dx), dyv[p]));
+        pre[p] = b0 + j < last[p] && pw[p] <= 0.0f && pw[p] >= pf;
+      }
+      if (!__any_sync(0xffffffffu, pre[0] || pre[1])) continue;
       float gv[NV];
 #pragma unroll
       for (int k = 0; k < NV; ++k) gv[k] = 0.0f;
       bool any = false;
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
-        const float dx = gs_sub(m.x, pxf), dy = gs_sub(m.y, pyf[p]);
-        const float power = gs_sub(gs_add(gs_mul(gs_mul(co.x, dx), dx), gs_mul(gs_mul(co.z, dy), dy)),
-                                   gs_mul(gs_mul(co.y, dx), dy));
+        const float dy = dyv[p];
+        const float power = pw[p];
         // Predicated (no per-pixel branches): lanes that do not composite
         // this Gaussian evaluate the same arithmetic and add zeros.  The
         // gradient needs e^power only to float accuracy, but the skip
         // decision alpha < 1/255 must be the forward's: take the hardware
         // exponential (relative error ~1e-7) and redo it exactly only when
         // alpha lands within 1e-5 of the threshold.
-        bool take = b0 + j < last[p] && power <= 0.0f && power >= pf;
+        bool take = pre[p];
         float G = __expf(take ? power : 0.0f);
         float alpha = gs_minf(GS_ALPHA_MAX, gs_mul(co.w, G));
         if (take && fabsf(alpha - GS_ALPHA_MIN) < 1e-5f * GS_ALPHA_MIN) {
@@ -504,7 +517,17 @@ __global__ void __launch_bounds__(kBwdThreads) k_raster_bwd(const RasterBwdArgs 
         T[p] = take ? Tn : T[p];
         R[p] = take ? R[p] + cd * aT : R[p];
       }
-      if (!__any_sync(0xffffffffu, any)) continue;
+      const unsigned takers = __ballot_sync(0xffffffffu, any);
+      if (!takers) continue;
+      if ((takers & (takers - 1u)) == 0u) {
+        // one lane composited: its sums are the warp's, no reduction
+        if (any) {
+#pragma unroll
+          for (int k = 0; k < NV; ++k)
+            if (k < 6 + a.cc) s_gw[warp][k][j] = gv[k];
+        }
+        continue;
+      }
 #pragma unroll
       for (int k8 = 0; k8 < NV8; k8 += 8) {
         const float t = warp_reduce8(gv + k8, lane);
