@@ -45,11 +45,17 @@ def parse_args():
     ap.add_argument("--views", type=int, default=None, help="override the view count (configs 3 and 4)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--rank-views", choices=["same", "ring"], default="same",
+                    help="multi-GPU C2: every rank renders the C2 camera (identical per-GPU work), or rank r "
+                         "renders azimuth 30 + 45 r (views of unequal cost)")
     ap.add_argument("--no-multiview", action="store_true",
                     help="skip the C4 render and C3 training measurements that follow the C2 headline")
     ap.add_argument("--mv-steps", type=int, default=2, help="timed steps of each multi-view measurement")
     ap.add_argument("--sync-allreduce", action="store_true",
-                    help="multi-GPU C2: wait for each step's gradient all-reduce before the next step")
+                    help="multi-GPU C2: every step waits for its own gradient exchange (no overlap)")
+    ap.add_argument("--exchange", choices=["screen", "allreduce"], default="screen",
+                    help="multi-GPU C2: all-to-all of the screen-space cotangents + view-batched per-Gaussian "
+                         "backward (reduce-scattered gradient), or an all-reduce of the parameter gradients")
     return ap.parse_args()
 
 
@@ -188,7 +194,7 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     scene = make_scene(args.config, n=args.n)
     cfg = scene.config
-    cam = view_camera(scene, rank)
+    cam = view_camera(scene, rank if args.rank_views == "ring" else 0)
     params = scene.torch_params(device=dev, requires_grad=True)
     model = GaussianModel(params, sh_degree=3)
     model.active_sh_degree = cfg.sh_degree
@@ -205,8 +211,17 @@ def run_ours(args, world, rank, local):
     # (GradientReducer, two flat buffers).  The last one is waited for before
     # the timed region closes.  --sync-allreduce makes every step wait for
     # its own all-reduce instead.
+    from mlx3d_b200.distributed import ScreenGradientExchange
+
     reducer = GradientReducer()
-    overlap = world > 1 and not args.sync_allreduce
+    screen = world > 1 and args.exchange == "screen"
+    exchange = ScreenGradientExchange()
+    overlap = world > 1 and not screen and not args.sync_allreduce
+    # screen exchange: step k's all-to-all runs on NCCL's stream under step
+    # k+1's forward; its per-Gaussian backward is launched once step k+1's
+    # forward is enqueued (the step has no optimizer, nothing reads the
+    # gradient earlier); the last one completes inside the timed region
+    screen_overlap = screen and not args.sync_allreduce
 
     def step(model_=model, target_=target):
         pl = list(model_.params.values())
@@ -215,7 +230,20 @@ def run_ours(args, world, rank, local):
         out = model_.render(cam, antialias=cfg.antialias)
         if overlap:
             reducer.launch()
+        if screen_overlap:
+            while exchange.in_flight():
+                exchange.finish()
         loss = l1_loss(out["image"], target_)
+        if screen:
+            # the gradient ends reduce-scattered: this rank holds the sum over
+            # all ranks' views for its slice of the Gaussians
+            with exchange.capture():
+                loss.backward()
+            if screen_overlap:
+                exchange.start()
+            else:
+                exchange.reduce()
+            return loss
         if overlap:
             with reducer.sink(pl):  # gradients land in the next flat all-reduce buffer
                 loss.backward()
@@ -232,6 +260,8 @@ def run_ours(args, world, rank, local):
     def drain():
         while reducer.in_flight():
             reducer.finish()
+        while exchange.in_flight():
+            exchange.finish()
 
     def barrier():
         if world > 1:
@@ -257,7 +287,11 @@ def run_ours(args, world, rank, local):
     launches = lib.gs_kernel_launch_count() - launches0
     ms_step = start.elapsed_time(end) / args.steps
     t = torch.tensor([ms_step], device=dev)
+    rank_ms = [ms_step]
     if world > 1:
+        every = torch.empty((world,), device=dev)
+        dist.all_gather_into_tensor(every, t)
+        rank_ms = [round(float(x), 4) for x in every.tolist()]
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_step = float(t.item())
 
@@ -284,6 +318,14 @@ def run_ours(args, world, rank, local):
     finally:
         nat.call = orig_call
     stages = {k: sum(a.elapsed_time(b) for a, b in v) / prof_steps for k, v in stage_ms.items()}
+    # this rank's device time inside library calls per step (its compute,
+    # without waits for other ranks), gathered for the line
+    comp = torch.tensor([sum(stages.values())], device=dev)
+    rank_compute = [round(float(comp.item()), 4)]
+    if world > 1:
+        every = torch.empty((world,), device=dev)
+        dist.all_gather_into_tensor(every, comp)
+        rank_compute = [round(float(x), 4) for x in every.tolist()]
     with torch.no_grad():
         out = model.render(cam, antialias=cfg.antialias)
         from mlx3d_b200.splatting.tiles import bin_gaussians
@@ -382,12 +424,22 @@ def run_ours(args, world, rank, local):
             "width": cam.width,
             "height": cam.height,
             "views_per_step": world,
+            "rank_views": ("every rank renders the C2 camera (identical per-GPU work)" if args.rank_views == "same"
+                           else "rank r renders azimuth 30 + 45 r (unequal per-view cost)") if world > 1 else None,
             "duplicates": d,
             "visible_gaussians": visible,
-            "parallelism": (f"views sharded over {world} GPU(s); per-Gaussian gradient all-reduce (NCCL, one "
-                            f"flat 59-float-per-Gaussian buffer per step, "
-                            + ("waited for by the same step)" if args.sync_allreduce else
-                               "overlapped with the next step's render; all complete inside the timed region)"))
+            "parallelism": ((f"views sharded over {world} GPU(s); screen-space cotangents (9 floats per "
+                             f"Gaussian) exchanged by one NCCL all-to-all per step, then one view-batched "
+                             f"per-Gaussian backward per rank over its 1/{world} of the Gaussians: the summed "
+                             f"gradient ends reduce-scattered across ranks")
+                            if screen else
+                            (f"views sharded over {world} GPU(s); per-Gaussian gradient all-reduce (NCCL, one "
+                             f"flat 59-float-per-Gaussian buffer per step, "
+                             + ("waited for by the same step)" if args.sync_allreduce else
+                                "overlapped with the next step's render; all complete inside the timed region)")))
+                           + ("" if not screen else ("; each step's exchange overlaps the next step's forward, the "
+                                                     "last completes inside the timed region" if screen_overlap
+                                                     else "; each step waits for its own exchange"))
                            if world > 1 else "single GPU",
             "l2": "no flush: per-step working set (parameters %.0f MB + gradients + image buffers) exceeds the "
                   "126 MB L2" % (sum(v.nbytes for v in scene.params.values()) / 1e6),
@@ -395,6 +447,8 @@ def run_ours(args, world, rank, local):
         "e2e": e2e,
         "gpu_launches": int(launches),
         "clocks": clk,
+        "rank_ms_per_step": rank_ms,
+        "rank_compute_ms_per_step": rank_compute,
         "stages_ms": stage_rows,
         "roofline": {
             "kernel": dom,

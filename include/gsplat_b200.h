@@ -161,6 +161,26 @@ int gs_preprocess_backward(const gs_camera* cam, const float* means, const float
                            float* g_opacities, float* g_sh_dc, float* g_sh_rest,
                            void* stream);
 
+/* View-batched VJP of gs_preprocess_forward: the gradient with respect to the
+ * raw inputs summed over n_views views of the same n Gaussians (the sum of
+ * n_views gs_preprocess_backward calls, in one pass over the parameters).
+ * cams: DEVICE array of n_views gs_camera.  g_screen: per view, rows of 9
+ * floats per Gaussian (dL/d means2d 2, conic 3, colour 3, effective opacity
+ * 1, as gs_rasterize_backward produces them), view v at g_screen +
+ * v * view_stride.  Outputs as gs_preprocess_backward (written, not added).
+ * Serves data parallelism over views: a rank that owns a slice of the
+ * Gaussians receives every rank's cotangents for that slice (all-to-all)
+ * and produces its slice of the summed gradient.  The reference has no
+ * multi-device path; its single-view counterpart is MLX autodiff through
+ * projection.py / sh.py / render.py:56-80. */
+int gs_preprocess_backward_views(const gs_camera* cams, int n_views, const float* means,
+                                 const float* quats, const float* scales, const float* opacities,
+                                 const float* sh_dc, int64_t sh_dc_stride, const float* sh_rest,
+                                 int64_t sh_rest_stride, int sh_degree, int64_t n, float blur, int antialias,
+                                 int flags, const float* g_screen, int64_t view_stride, float* g_means,
+                                 float* g_quats, float* g_scales, float* g_opacities, float* g_sh_dc,
+                                 float* g_sh_rest, void* stream);
+
 /* ------------------------------------------------------------------- binning
  * bin_gaussians (src/mlx3d/splatting/tiles.py:19-182), split where the
  * reference itself synchronises with the host (tiles.py:68):

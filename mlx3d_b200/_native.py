@@ -94,6 +94,12 @@ _SIGS = {
         + [_P] * 6
         + [_P],
     ),
+    "gs_preprocess_backward_views": (
+        c_int,
+        [_P, c_int, _P, _P, _P, _P, _P, c_int64, _P, c_int64, c_int, c_int64, c_float, c_int, c_int, _P, c_int64]
+        + [_P] * 6
+        + [_P],
+    ),
     "gs_tile_counts": (c_int, [_P, _P, c_int64, c_int, c_int, _P, _P]),
     "gs_bin_workspace_n_bytes": (c_size_t, [c_int64]),
     "gs_bin_workspace_d_bytes": (c_size_t, [c_int64]),

@@ -585,6 +585,134 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd(const PreBwdArgs g
   }
 }
 
+// ------------------------------------------------- view-batched backward
+// The VJP of gs_preprocess_forward summed over several views of the same
+// Gaussians: gradient = sum over views v of VJP_v(cotangents_v).  Used when
+// the views' screen-space cotangents (9 floats per Gaussian and view:
+// means2d 2, conic 3, colour 3, effective opacity 1) have been gathered on
+// one device, e.g. a rank that owns a slice of the Gaussians after an
+// all-to-all of every rank's cotangents for that slice.  One thread per
+// Gaussian walks the views: the parameter rows are read once, each view's
+// projection is recomputed (as the single-view backward does), and the SH
+// coefficient gradients sum in shared memory (48 floats per row, odd pitch).
+constexpr int kViewsGradPitch = 49;
+
+struct PreBwdViewsArgs {
+  PreFwdArgs f;                // cam unused
+  const gs_camera* cams;       // device array of n_views cameras
+  int n_views;
+  const float* g_screen;       // view v, Gaussian i: g_screen + v * view_stride + 9 i
+  int64_t view_stride;
+  float *g_means, *g_quats, *g_scales, *g_opac, *g_sh_dc, *g_sh_rest;
+};
+
+__global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd_views(const PreBwdViewsArgs g) {
+  extern __shared__ __align__(16) float smem[];
+  const PreFwdArgs& a = g.f;
+  const int64_t base = (int64_t)blockIdx.x * kPreBlock;
+  const int rows = (int)min((int64_t)kPreBlock, a.n - base);
+  const int nb = a.sh_degree >= 0 ? (a.sh_degree + 1) * (a.sh_degree + 1) : 0;
+  const int rest_len = nb > 1 ? (nb - 1) * 3 : 0;
+  const bool sh = nb > 0;
+  const float* g_means = a.means + base * 3;
+  const float* g_scales = a.scales + base * 3;
+  const float* g_dc = sh ? a.sh_dc + base * a.dc_stride : nullptr;
+  const float* g_rest = (sh && rest_len) ? a.sh_rest + base * a.rest_stride : nullptr;
+  const int mld = stage_pitch(g_means, 3, 3), sld = stage_pitch(g_scales, 3, 3);
+  const int dld = g_dc ? stage_pitch(g_dc, a.dc_stride, 3) : 3;
+  const int rest_ld = g_rest ? stage_pitch(g_rest, a.rest_stride, rest_len) : 1;
+  float* s_means = smem;
+  float* s_scales = s_means + kPreBlock * 4;
+  float* s_dc = s_scales + kPreBlock * 4;
+  float* s_rest = s_dc + kPreBlock * 4;
+  float* s_g = s_rest + kPreBlock * (rest_len | 1);  // SH gradient rows: dc 3, rest 45
+  __shared__ unsigned long long s_bar;
+  const StagePlan plan(g_means, g_scales, g_dc, a.dc_stride, g_rest, a.rest_stride, rest_len, rows);
+  plan.issue(&s_bar, s_means, g_means, s_scales, g_scales, s_dc, g_dc, a.dc_stride, s_rest, g_rest, a.rest_stride,
+             rest_len, rows);
+  const int li = threadIdx.x;
+  const int64_t i = base + li;
+  float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+  float o_raw = 0.f;
+  if (li < rows) {
+    q = __ldg(reinterpret_cast<const float4*>(a.quats) + i);
+    o_raw = __ldg(a.opac + i);
+  }
+  if (sh)
+    for (int k = 0; k < kViewsGradPitch; ++k) s_g[li * kViewsGradPitch + k] = 0.0f;
+  if (!plan.wait(&s_bar)) return;
+  if (li < rows) {
+    const float r0 = s_scales[li * sld + 0], r1 = s_scales[li * sld + 1], r2 = s_scales[li * sld + 2];
+    float s0 = r0, s1 = r1, s2 = r2;
+    if (a.flags & GS_ACT_EXP_SCALES) {
+      s0 = gs_expf(r0);
+      s1 = gs_expf(r1);
+      s2 = gs_expf(r2);
+    }
+    const float m0 = s_means[li * mld + 0], m1 = s_means[li * mld + 1], m2 = s_means[li * mld + 2];
+    float o = o_raw;
+    if (a.flags & GS_ACT_SIGMOID_OPACITY) o = gs_sigmoidf(o_raw);
+    float gm[3] = {0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f}, gsc[3] = {0.f, 0.f, 0.f}, go = 0.f;
+    for (int v = 0; v < g.n_views; ++v) {
+      const gs_camera& cam = g.cams[v];
+      const float* cot = g.g_screen + v * g.view_stride + 9 * (int64_t)i;
+      const float gu = __ldg(cot + 0), gv = __ldg(cot + 1);
+      const float gA = __ldg(cot + 2), gB = __ldg(cot + 3), gC = __ldg(cot + 4);
+      const float goo = __ldg(cot + 8);
+      // opacities_out = act(opacity) * compensation   (render.py:75)
+      Proj p;
+      project_one(cam, m0, m1, m2, q.x, q.y, q.z, q.w, s0, s1, s2, a.blur, a.aa != 0, p);
+      go += goo * p.comp;
+      float gmv[3], gqv[4], gsv[3];
+      project_vjp(cam, m0, m1, m2, q.x, q.y, q.z, q.w, s0, s1, s2, a.blur, a.aa != 0, gu, gv, gA, gB, gC, 0.0f,
+                  goo * o, gmv, gqv, gsv);
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        gm[k] += gmv[k];
+        gsc[k] += gsv[k];
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) gq[k] += gqv[k];
+      if (sh) {
+        float dx, dy, dz;
+        view_dir(cam, m0, m1, m2, dx, dy, dz);
+        float bs[16];
+        sh_basis(a.sh_degree, dx, dy, dz, bs);
+#pragma unroll
+        for (int ch = 0; ch < 3; ++ch) {
+          float r = gs_mul(bs[0], s_dc[li * dld + ch]);
+          for (int k = 1; k < nb; ++k) r = gs_add(r, gs_mul(bs[k], s_rest[li * rest_ld + (k - 1) * 3 + ch]));
+          r = gs_add(r, 0.5f);
+          const float gcol = r > 0.0f ? __ldg(cot + 5 + ch) : 0.0f;
+          s_g[li * kViewsGradPitch + ch] += bs[0] * gcol;
+          for (int k = 1; k < nb; ++k) s_g[li * kViewsGradPitch + 3 + (k - 1) * 3 + ch] += bs[k] * gcol;
+        }
+      }
+    }
+    if (a.flags & GS_ACT_SIGMOID_OPACITY) go = go * o * (1.0f - o);
+    if (a.flags & GS_ACT_EXP_SCALES) {
+      gsc[0] *= s0;
+      gsc[1] *= s1;
+      gsc[2] *= s2;
+    }
+    g.g_opac[i] = go;
+    g.g_means[3 * i + 0] = gm[0];
+    g.g_means[3 * i + 1] = gm[1];
+    g.g_means[3 * i + 2] = gm[2];
+    reinterpret_cast<float4*>(g.g_quats)[i] = make_float4(gq[0], gq[1], gq[2], gq[3]);
+    g.g_scales[3 * i + 0] = gsc[0];
+    g.g_scales[3 * i + 1] = gsc[1];
+    g.g_scales[3 * i + 2] = gsc[2];
+  }
+  if (sh) {
+    __syncthreads();
+    unstage_rows<kPreBlock>(g.g_sh_dc + base * a.dc_stride, a.dc_stride, s_g, kViewsGradPitch, 3, rows);
+    if (rest_len > 0)
+      unstage_rows<kPreBlock>(g.g_sh_rest + base * a.rest_stride, a.rest_stride, s_g + 3, kViewsGradPitch,
+                              rest_len, rows);
+  }
+}
+
 // ------------------------------------------------------------ eval_sh kernels
 // Standalone eval_sh (N, K, C) with explicit directions; one thread per
 // (Gaussian, channel) pair.
@@ -789,6 +917,49 @@ int gs_preprocess_backward(const gs_camera* cam, const float* means, const float
   const size_t sm = pre_smem_bytes(deg, true);
   k_preprocess_bwd<<<(unsigned)ceil_div(n, kPreBlock), kPreBlock, sm, as_stream(stream)>>>(g);
   return check_launch("k_preprocess_bwd");
+}
+
+int gs_preprocess_backward_views(const gs_camera* cams, int n_views, const float* means,
+                                 const float* quats, const float* scales, const float* opacities,
+                                 const float* sh_dc, int64_t sh_dc_stride, const float* sh_rest,
+                                 int64_t sh_rest_stride, int sh_degree, int64_t n, float blur, int antialias,
+                                 int flags, const float* g_screen, int64_t view_stride, float* g_means,
+                                 float* g_quats, float* g_scales, float* g_opacities, float* g_sh_dc,
+                                 float* g_sh_rest, void* stream) {
+  clear_error();
+  if (n < 0) return set_error(GS_ERR_INVALID_ARG, "n must be >= 0");
+  if (n_views < 0) return set_error(GS_ERR_INVALID_ARG, "n_views must be >= 0");
+  if (n == 0) return GS_OK;
+  if (!cams && n_views > 0) return set_error(GS_ERR_INVALID_ARG, "cams is NULL");
+  if (!means || !quats || !scales || !opacities || !g_means || !g_quats || !g_scales || !g_opacities ||
+      (n_views > 0 && !g_screen))
+    return set_error(GS_ERR_INVALID_ARG, "gs_preprocess_backward_views: NULL pointer");
+  if (view_stride < 9 * n && n_views > 1)
+    return set_error(GS_ERR_INVALID_ARG, "view_stride %lld is below 9 n = %lld", (long long)view_stride,
+                     (long long)(9 * n));
+  if (!aligned(quats, 16) || !aligned(g_quats, 16))
+    return set_error(GS_ERR_INVALID_ARG, "quats / g_quats must be 16-byte aligned");
+  const int deg = sh_dc ? sh_degree : -1;
+  if (sh_dc && (sh_degree < 0 || sh_degree > 3))
+    return set_error(GS_ERR_INVALID_ARG, "sh_degree must be in [0, 3] (got %d)", sh_degree);
+  if (sh_dc && (!g_sh_dc || (sh_degree > 0 && (!sh_rest || !g_sh_rest))))
+    return set_error(GS_ERR_INVALID_ARG, "gs_preprocess_backward_views: NULL SH pointer");
+  PreBwdViewsArgs g{};
+  PreFwdArgs& a = g.f;
+  a.means = means; a.quats = quats; a.scales = scales; a.opac = opacities;
+  a.sh_dc = sh_dc; a.sh_rest = sh_rest; a.dc_stride = sh_dc_stride; a.rest_stride = sh_rest_stride;
+  a.sh_degree = deg; a.n = n; a.blur = blur; a.aa = antialias && blur > 0.0f; a.flags = flags; a.fused = 1;
+  g.cams = cams; g.n_views = n_views; g.g_screen = g_screen; g.view_stride = view_stride;
+  g.g_means = g_means; g.g_quats = g_quats; g.g_scales = g_scales; g.g_opac = g_opacities;
+  g.g_sh_dc = g_sh_dc; g.g_sh_rest = g_sh_rest;
+  const size_t sm = pre_smem_bytes(deg, true) + (deg >= 0 ? sizeof(float) * kPreBlock * kViewsGradPitch : 0);
+  if (sm > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(k_preprocess_bwd_views, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)sm);
+    if (e != cudaSuccess) return set_error(GS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+  }
+  k_preprocess_bwd_views<<<(unsigned)ceil_div(n, kPreBlock), kPreBlock, sm, as_stream(stream)>>>(g);
+  return check_launch("k_preprocess_bwd_views");
 }
 
 int gs_eval_sh_forward(int degree, const float* sh, int64_t n, int k, int channels,

@@ -15,7 +15,8 @@ import time
 import torch
 import torch.distributed as dist
 
-__all__ = ["shard_views", "allreduce_gradients", "GradientReducer", "PeerLost", "PeerMonitor", "world"]
+__all__ = ["shard_views", "allreduce_gradients", "GradientReducer", "ScreenGradientExchange", "PeerLost",
+           "PeerMonitor", "world"]
 
 
 def world() -> tuple[int, int]:
@@ -172,6 +173,156 @@ class GradientReducer:
         if work is not True:
             work.wait()  # the current stream waits for the collective
         return buf
+
+
+class ScreenGradientExchange:
+    """Sums per-Gaussian gradients over ranks by exchanging screen-space
+    cotangents instead of parameter gradients.
+
+    Every rank renders its own view of the same (replicated) Gaussians.  The
+    parameter gradient of a view is a per-Gaussian function of the view's
+    screen-space cotangents, 9 floats per Gaussian (dL/d means2d, conic,
+    colour, effective opacity), while the gradient itself has 59 floats at
+    SH degree 3.  So instead of all-reducing 59 N floats, the ranks exchange
+    the 9-float cotangents with one all-to-all, Gaussian slice r going to
+    rank r (9 N floats sent per rank in total), and rank r runs one
+    view-batched per-Gaussian backward (``gs_preprocess_backward_views``)
+    over its slice and all ranks' views.  Rank r ends with the summed
+    gradient of Gaussians [lo_r, hi_r) -- a reduce-scatter result, as a
+    sharded optimizer consumes it.
+
+    Usage: ``with ex.capture(): loss.backward()`` (the fused render's
+    backward stops after the compositor and hands its cotangents over; the
+    parameters get no ``.grad``), then ``ex.reduce()``.  Pipelines in which
+    nothing reads the gradient before the next view is rendered can split
+    it: ``start()`` launches the all-to-all on NCCL's stream without making
+    the current stream wait, and ``finish()`` (called after the next view's
+    forward is enqueued) waits for it and runs the per-Gaussian backward;
+    two exchanges may be in flight.  The loss may depend on the rendered
+    image and alpha only; ranks must render with the same antialias / SH
+    settings."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self._captured = None
+        self._slots: list[tuple | None] = [None, None]
+        self._next = 0
+        self._pending: list[dict] = []
+
+    @contextlib.contextmanager
+    def capture(self):
+        from .splatting import render as _render
+
+        def hook(cfg, cot, params):
+            self._captured = (cfg, cot, params)
+
+        _render.set_screen_grad_hook(hook)
+        try:
+            yield self
+        finally:
+            _render.set_screen_grad_hook(None)
+
+    @staticmethod
+    def slice_of(n: int, rank: int, ws: int) -> tuple[int, int]:
+        """[lo, hi) of the Gaussians rank ``rank`` reduces (equal slices of
+        ceil(n / ws), the last one shorter)."""
+        per = -(-n // ws) if ws > 0 else n
+        lo = min(n, rank * per)
+        return lo, min(n, lo + per)
+
+    def in_flight(self) -> int:
+        return len(self._pending)
+
+    def _slot(self, n, ws, dev):
+        per = -(-n // ws)
+        slot = self._slots[self._next]
+        if slot is None or slot[0].shape[0] != per * ws or slot[0].device != dev:
+            slot = (torch.zeros((per * ws, 9), device=dev, dtype=torch.float32),
+                    torch.empty((ws, per, 9), device=dev, dtype=torch.float32))
+            self._slots[self._next] = slot
+        self._next ^= 1
+        return slot
+
+    def start(self) -> None:
+        """Pack the captured cotangents and launch the all-to-all (and the
+        camera all-gather) without waiting for them."""
+        if self._captured is None:
+            raise RuntimeError("ScreenGradientExchange: no backward was captured")
+        if len(self._pending) >= 2:
+            raise RuntimeError("ScreenGradientExchange: two exchanges in flight; finish() one first")
+        cfg, (g_m2d, g_con, g_col, g_op), params = self._captured
+        self._captured = None
+        rank, ws = world()
+        means = params[0]
+        n = means.shape[0]
+        dev = means.device
+        send, recv = self._slot(n, ws, dev)
+        torch.cat([g_m2d, g_con, g_col, g_op.reshape(-1, 1)], dim=1, out=send[:n])
+        raw = torch.frombuffer(bytearray(bytes(cfg.cam)), dtype=torch.uint8)
+        # this rank's camera as device bytes (pinned source: no host synchronisation)
+        cam_bytes = raw.pin_memory().to(dev, non_blocking=True) if dev.type == "cuda" else raw
+        works = []
+        if ws > 1:
+            works.append(dist.all_to_all_single(recv.view(-1), send.view(-1), group=self.group, async_op=True))
+            cams = torch.empty((ws * cam_bytes.numel(),), device=dev, dtype=torch.uint8)
+            works.append(dist.all_gather_into_tensor(cams, cam_bytes, group=self.group, async_op=True))
+        else:
+            recv.view(-1).copy_(send.view(-1))
+            cams = cam_bytes
+        self._pending.append({"cfg": cfg, "params": params, "recv": recv, "cams": cams, "works": works,
+                              "per": -(-n // ws), "ws": ws, "rank": rank})
+
+    def finish(self) -> dict:
+        """Wait (on the current stream) for the oldest exchange and run the
+        view-batched backward of this rank's slice.  Returns {"range": (lo,
+        hi), "means", "quats", "scales", "opacities", "sh_a", "sh_b"}
+        (gradient slices; sh_b is None at SH degree 0)."""
+        from . import _native as nat
+        from .splatting.render import _sh_layout
+
+        if not self._pending:
+            raise RuntimeError("ScreenGradientExchange: nothing in flight")
+        e = self._pending.pop(0)
+        for w in e["works"]:
+            w.wait()
+        cfg = e["cfg"]
+        means, quats, scales, opac, sh_a, sh_b = e["params"]
+        n, ws, per = means.shape[0], e["ws"], e["per"]
+        dev = means.device
+        lo, hi = self.slice_of(n, e["rank"], ws)
+        m = hi - lo
+        f32 = dict(device=dev, dtype=torch.float32)
+        out = {"range": (lo, hi), "means": torch.empty((m, 3), **f32), "quats": torch.empty((m, 4), **f32),
+               "scales": torch.empty((m, 3), **f32), "opacities": torch.empty((m,), **f32),
+               "sh_a": torch.empty((m,) + tuple(sh_a.shape[1:]), **f32),
+               "sh_b": None if sh_b is None else torch.empty((m,) + tuple(sh_b.shape[1:]), **f32)}
+        if m == 0:
+            return out
+        dc, dcs, rest, rests = _sh_layout(cfg, sh_a, sh_b)
+        g_dc = out["sh_a"].data_ptr()
+        g_rest = None
+        if cfg.sh_mode == "full":
+            g_rest = (g_dc + 12) if sh_a.shape[1] > 1 else None
+            if sh_a.shape[1] > (cfg.sh_degree + 1) ** 2:
+                out["sh_a"].zero_()
+        elif sh_b is not None and sh_b.numel():
+            g_rest = out["sh_b"].data_ptr()
+            if sh_b.shape[1] + 1 > (cfg.sh_degree + 1) ** 2:
+                out["sh_b"].zero_()
+        off = lambda p, stride: None if p is None else p + 4 * lo * stride  # noqa: E731
+        nat.call(
+            "gs_preprocess_backward_views", e["cams"].data_ptr(), ws, nat.ptr(means[lo:hi]),
+            nat.ptr(quats[lo:hi]), nat.ptr(scales[lo:hi]), nat.ptr(opac[lo:hi]), off(dc, dcs), dcs,
+            off(rest, rests), rests, cfg.sh_degree, m, cfg.blur, int(cfg.antialias), cfg.flags,
+            e["recv"].data_ptr(), per * 9, nat.ptr(out["means"]), nat.ptr(out["quats"]), nat.ptr(out["scales"]),
+            nat.ptr(out["opacities"]), g_dc, g_rest, nat.stream(),
+        )
+        return out
+
+    def reduce(self) -> dict:
+        """start() + finish() of the captured backward."""
+        self.start()
+        return self.finish()
 
 
 class PeerLost(RuntimeError):

@@ -131,6 +131,12 @@ class _Render(torch.autograd.Function):
             g_m2d += g_means2d_out
         if cfg.probe is not None:
             cfg.probe.copy_(g_m2d)
+        if _screen_hook is not None and cfg.sh_mode != "colors":
+            if g_depths_out is not None or g_comp_out is not None:
+                raise ValueError("screen-space gradient exchange: the loss may depend on the image and alpha "
+                                 "only (depths / compensation have cotangents)")
+            _screen_hook(cfg, (g_m2d, g_con, g_col, g_op), (means, quats, scales, opacities, sh_a, sh_b))
+            return None, None, None, None, None, None, None, None, None
         g_means = _grad_like("means", means)
         g_quats = _grad_like("quats", quats)
         g_scales = _grad_like("scales", scales)
@@ -171,6 +177,21 @@ class _Render(torch.autograd.Function):
 # buffer.  A module global, not thread-local: autograd runs CUDA backward
 # functions on its own device thread.
 _grad_sink = None
+
+
+# Optional consumer of the next backward's screen-space cotangents: a
+# callable (cfg, (g_means2d, g_conics, g_colors, g_opacities_out), (means,
+# quats, scales, opacities, sh_a, sh_b)).  When set, the fused render's
+# backward stops after the compositor backward, hands the cotangents over
+# and returns no parameter gradients: the consumer (e.g.
+# mlx3d_b200.distributed.ScreenGradientExchange) runs the per-Gaussian
+# backward itself.  Module global for the same reason as _grad_sink.
+_screen_hook = None
+
+
+def set_screen_grad_hook(fn) -> None:
+    global _screen_hook
+    _screen_hook = fn
 
 
 def set_grad_sink(fn) -> None:

@@ -202,3 +202,68 @@ def test_peer_monitor_single_rank_and_store_failure():
         lone.beat(1)
     with pytest.raises(PeerLost, match="unreachable"):
         PeerMonitor(store=BrokenStore(), rank=0, world_size=2, timeout=0.1).beat(0)
+
+
+def _exchange_worker(rank, world_size, port, results):
+    """ScreenGradientExchange host logic on gloo ranks (CPU): padding, the
+    all-to-all of the 9-float cotangent rows, the camera all-gather and the
+    slice handed to the view-batched backward (the kernel call itself is
+    recorded instead of run: there is no GPU here)."""
+    import types
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world_size)
+    try:
+        from mlx3d_b200 import _native as nat
+        from mlx3d_b200.distributed import ScreenGradientExchange
+
+        n = 7  # not a multiple of the world size: the last slice is shorter
+        cam = nat.GsCamera()
+        cam.fx = float(rank + 1)
+        cfg = types.SimpleNamespace(cam=cam, sh_mode="split", sh_degree=1, blur=0.3, antialias=False, flags=3)
+        means, quats, scales = torch.zeros(n, 3), torch.zeros(n, 4), torch.zeros(n, 3)
+        opac, sh_dc, sh_rest = torch.zeros(n), torch.zeros(n, 1, 3), torch.zeros(n, 3, 3)
+        # cotangent row i of rank r: [100 r + i, ...] so every received row names its origin
+        base = (100.0 * rank + torch.arange(n, dtype=torch.float32)).reshape(n, 1)
+        cot = (base.repeat(1, 2), base.repeat(1, 3) + 0.1, base.repeat(1, 3) + 0.2, base[:, 0] + 0.3)
+        calls = []
+        nat.call = lambda name, *a: calls.append((name, a))
+        nat.stream = lambda: None
+        ex = ScreenGradientExchange()
+        ex._captured = (cfg, cot, (means, quats, scales, opac, sh_dc, sh_rest))
+        out = ex.reduce()
+        name, a = calls[0]
+        lo, hi = out["range"]
+        recv = ex._slots[0][1].clone()
+        results[rank] = (name, lo, hi, a[1], recv.tolist(), a[11], a[16])
+    finally:
+        dist.destroy_process_group()
+
+
+def test_two_rank_screen_gradient_exchange_routes_rows_by_slice():
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, results)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+            assert p.exitcode == 0
+        res = {r: results[r] for r in (0, 1)}
+    per = 4  # ceil(7 / 2)
+    for r in (0, 1):
+        name, lo, hi, n_views, recv, n_slice, view_stride = res[r]
+        assert name == "gs_preprocess_backward_views" and n_views == 2
+        assert (lo, hi) == ((0, 4) if r == 0 else (4, 7)) and n_slice == hi - lo and view_stride == per * 9
+        for v in (0, 1):  # view v's block holds rank v's rows of this slice, padded with zeros
+            for k in range(per):
+                row = recv[v][k]
+                i = lo + k
+                if i < 7:
+                    assert row[0] == 100.0 * v + i and abs(row[2] - (100.0 * v + i + 0.1)) < 1e-4
+                    assert abs(row[8] - (100.0 * v + i + 0.3)) < 1e-4
+                else:
+                    assert row == [0.0] * 9
