@@ -249,7 +249,8 @@ class GaussianModel:
     def densify_and_prune(self, grad_accum: torch.Tensor, grad_count: torch.Tensor,
                           grad_threshold: float = 0.0002, scene_extent: float = 1.0,
                           percent_dense: float = 0.01, min_opacity: float = 0.005,
-                          return_optimizer_state: bool = False, generator: torch.Generator | None = None) -> dict:
+                          return_optimizer_state: bool = False, generator: torch.Generator | None = None,
+                          samples: torch.Tensor | None = None) -> dict:
         """Adaptive density control of the 3DGS paper (model.py:406-480).
 
         Average screen-space gradient = grad_accum / max(grad_count, 1); rows
@@ -260,7 +261,9 @@ class GaussianModel:
         and rows larger than half the scene extent are pruned.  The kept rows
         come first, then the clones, then the split pairs.  Returns the counts
         (and, with ``return_optimizer_state``, the kept indices and the number
-        of appended rows, for resizing optimizer moments)."""
+        of appended rows, for resizing optimizer moments).  ``samples``
+        ((2 * splits, 3) standard normal draws, pair-major) replaces the
+        draws from ``generator``."""
         from .projection import quat_to_rotmat
 
         dev = self.params["means"].device
@@ -278,7 +281,11 @@ class GaussianModel:
             if split_idx.numel() > 0:
                 R = quat_to_rotmat(p["quats"][split_idx])
                 s = scales[split_idx]
-                samples = torch.randn((split_idx.numel() * 2, 3), device=dev, dtype=s.dtype, generator=generator)
+                if samples is None:
+                    samples = torch.randn((split_idx.numel() * 2, 3), device=dev, dtype=s.dtype, generator=generator)
+                elif samples.shape != (split_idx.numel() * 2, 3):
+                    raise ValueError(f"samples must have shape ({split_idx.numel() * 2}, 3)")
+                samples = samples.to(device=dev, dtype=s.dtype)
                 samples = samples * s.repeat_interleave(2, dim=0)
                 offsets = torch.einsum("nij,nj->ni", R.repeat_interleave(2, dim=0), samples)
                 splits = {k: v[split_idx].repeat_interleave(2, dim=0) for k, v in p.items()}
@@ -299,13 +306,15 @@ class GaussianModel:
 
     def relocate_mcmc(self, grad_accum: torch.Tensor, grad_count: torch.Tensor, relocate_frac: float = 0.02,
                       min_opacity: float = 0.01, jitter_scale: float = 0.25,
-                      generator: torch.Generator | None = None) -> dict:
+                      generator: torch.Generator | None = None, noise: torch.Tensor | None = None) -> dict:
         """Fixed-budget relocation (model.py:482-531): up to
         ``relocate_frac * N`` underused rows (opacity below ``min_opacity`` or
         never visible; the least opaque rows when none is underused) are
         overwritten by copies of the highest-gradient other rows, with means
         jittered by ``jitter_scale`` times the source scales, the opacity
-        reset to logit(0.05) and log-scales reduced by log 1.6.  N is kept."""
+        reset to logit(0.05) and log-scales reduced by log 1.6.  N is kept.
+        ``noise`` ((k, 3) standard normal draws, in the order of the returned
+        ``_moved_idx``) replaces the draws from ``generator``."""
         n = self.num_gaussians
         max_relocate = int(max(0.0, min(relocate_frac, 1.0)) * n)
         if max_relocate <= 0 or n <= 1:
@@ -332,8 +341,9 @@ class GaussianModel:
                 arr = arr.detach()
                 values = arr[src].clone()
                 if name == "means" and jitter_scale > 0:
-                    noise = torch.randn(values.shape, device=dev, dtype=values.dtype, generator=generator)
-                    values = values + noise * source_scales * float(jitter_scale)
+                    z = (torch.randn(values.shape, device=dev, dtype=values.dtype, generator=generator)
+                         if noise is None else noise.to(device=dev, dtype=values.dtype).reshape(values.shape))
+                    values = values + z * source_scales * float(jitter_scale)
                 elif name == "opacities":
                     values = torch.full_like(values, math.log(0.05 / 0.95))
                 elif name == "scales":

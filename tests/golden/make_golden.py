@@ -12,6 +12,9 @@ reference modules are imported unmodified from its checkout:
 * ``splatting/tiles.py``  ``bin_gaussians`` (plain and ``conics`` refinement)
 * ``splatting/reference.py``  ``render_gaussians_reference`` (the naive
   O(N H W) renderer the reference's tests use as their oracle)
+* ``splatting/model.py``  ``GaussianModel.densify_and_prune`` and
+  ``relocate_mcmc`` (density control; numpy's global generator seeded, the
+  split draws stored beside the outputs)
 
 What this pins: the float32 operation order of those modules (every output
 but the naive renderer's is compared bit for bit).  What it cannot pin:
@@ -54,6 +57,16 @@ def install_reference(ref_root: Path):
         sys.modules[name] = m
     cams = importlib.import_module("mlx3d.cameras")  # its __init__ imports cameras.py only
     mods = {k: importlib.import_module(f"mlx3d.splatting.{k}") for k in ("projection", "sh", "tiles", "reference")}
+    # model.py imports IO, mesh structures and the Metal renderer at module
+    # level; density control uses none of them, so they are stubbed.
+    for name, attrs in (("mlx3d.io", ("load_ply", "save_ply")), ("mlx3d.structures", ("Meshes",)),
+                        ("mlx3d.splatting.render", ("render_gaussian_depth", "render_gaussian_features",
+                                                    "render_gaussians"))):
+        m = types.ModuleType(name)
+        for a in attrs:
+            setattr(m, a, None)
+        sys.modules[name] = m
+    mods["model"] = importlib.import_module("mlx3d.splatting.model")
     return cams, mods
 
 
@@ -91,6 +104,59 @@ def scene_inputs():
     eye = (4 * np.cos(e) * np.sin(a), 4 * np.sin(e), -4 * np.cos(e) * np.cos(a))
     out.append(("c1_3k", tuple(float(v) for v in eye), 60.0, 320, 180, means, quats, scales, opac, colors))
     return out
+
+
+def density_params(seed: int, n: int):
+    """Seeded raw parameters (SH degree 1) with a spread of scales and opacities."""
+    rng = np.random.Generator(np.random.PCG64(seed))
+    return {
+        "means": rng.normal(size=(n, 3)).astype(np.float32),
+        "scales": rng.normal(-3.0, 1.0, size=(n, 3)).astype(np.float32),
+        "quats": rng.normal(size=(n, 4)).astype(np.float32),
+        "opacities": rng.normal(0.0, 3.0, size=(n,)).astype(np.float32),
+        "sh_dc": rng.normal(size=(n, 1, 3)).astype(np.float32),
+        "sh_rest": rng.normal(0, 0.1, size=(n, 3, 3)).astype(np.float32),
+    }, rng
+
+
+def density_cases(model_m, data):
+    """densify_and_prune and relocate_mcmc of model.py:406-531 on the stand-in."""
+    import mlx_numpy as mx
+
+    names = ("means", "scales", "quats", "opacities", "sh_dc", "sh_rest")
+    # densify: 600 rows, a third above the gradient threshold
+    params, rng = density_params(200, 600)
+    grad_accum = rng.uniform(0.0, 0.0006, size=(600,)).astype(np.float32)
+    grad_count = rng.integers(0, 4, size=(600,)).astype(np.float32)
+    m = model_m.GaussianModel({k: mx.array(v) for k, v in params.items()}, sh_degree=1)
+    np.random.seed(1234)
+    stats = m.densify_and_prune(mx.array(grad_accum), mx.array(grad_count), grad_threshold=0.0002,
+                                scene_extent=3.0, percent_dense=0.02, min_opacity=0.005,
+                                return_optimizer_state=True)
+    np.random.seed(1234)
+    z = np.random.normal(size=(2 * stats["split"], 3))
+    p = "density/"
+    for k in names:
+        data[p + "in_" + k] = params[k]
+        data[p + "out_" + k] = np.asarray(m.params[k])
+    data[p + "grad_accum"], data[p + "grad_count"] = grad_accum, grad_count
+    data[p + "split_samples"] = z
+    data[p + "keep_idx"] = np.asarray(stats["_keep_idx"], np.int32)
+    data[p + "counts"] = np.array([stats["cloned"], stats["split"], stats["pruned"]], np.int64)
+    # relocation: 500 rows, some never visible or nearly transparent, no jitter
+    params, rng = density_params(201, 500)
+    grad_accum = rng.uniform(0.0, 0.001, size=(500,)).astype(np.float32)
+    grad_count = rng.integers(0, 3, size=(500,)).astype(np.float32)
+    m = model_m.GaussianModel({k: mx.array(v) for k, v in params.items()}, sh_degree=1)
+    st = m.relocate_mcmc(mx.array(grad_accum), mx.array(grad_count), relocate_frac=0.05, min_opacity=0.01,
+                         jitter_scale=0.0)
+    p = "mcmc/"
+    for k in names:
+        data[p + "in_" + k] = params[k]
+        data[p + "out_" + k] = np.asarray(m.params[k])
+    data[p + "grad_accum"], data[p + "grad_count"] = grad_accum, grad_count
+    data[p + "moved_idx"] = np.sort(np.asarray(st["_moved_idx"], np.int64))
+    data[p + "relocated"] = np.array([st["relocated"]], np.int64)
 
 
 def main(ref_root: str):
@@ -149,6 +215,7 @@ def main(ref_root: str):
                                                      antialias=aa)
                 data[p + f"naive_aa{int(aa)}/image"] = np.asarray(r["image"], np.float32)
                 data[p + f"naive_aa{int(aa)}/final_T"] = np.asarray(r["final_T"], np.float32)
+    density_cases(mods["model"], data)
     np.savez_compressed(OUT, **data)
     print(f"wrote {OUT} ({OUT.stat().st_size / 1e6:.2f} MB, {len(data)} arrays)")
 

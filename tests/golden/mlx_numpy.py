@@ -1,5 +1,6 @@
 """A float32 numpy stand-in for the parts of ``mlx.core`` that mlx3D's
-projection, SH, binning, camera and naive-renderer modules call.
+projection, SH, binning, camera, naive-renderer and density-control modules
+call.
 
 Test infrastructure only: ``make_golden.py`` installs it as ``mlx.core`` so
 that the reference's own Python source (imported from the reference checkout
@@ -10,6 +11,9 @@ a*b+c into FMAs), with MLX's typing rules where they differ from numpy's:
 * Python scalars and lists become float32 / int32 arrays (MLX's defaults);
 * ``cumsum`` keeps the input's integer type;
 * ``argsort`` is stable (MLX's tie order is not documented: unpinned);
+  ``argpartition`` is numpy's (the order inside MLX's selection is not
+  documented either: only the selected set is compared);
+* ``random.normal`` draws from numpy's global generator;
 * ``linalg.norm`` over an axis and small matrix products sum their terms
   left to right without FMA (MLX's reduction order is not documented:
   unpinned);
@@ -155,6 +159,23 @@ arctan = _ew(np.arctan)
 sin = _ew(np.sin)
 cos = _ew(np.cos)
 exp = _ew(np.exp)
+
+
+def sigmoid(a):
+    a = _f32(_np(a))
+    return _wrap((1.0 / (1.0 + np.exp(-a))).astype(a.dtype))
+
+
+def argpartition(a, kth, axis=-1):
+    return _wrap(np.argpartition(_np(a), kth, axis=axis).astype(np.int32))
+
+
+class random:  # noqa: N801
+    """Draws from numpy's global generator (seeded by the caller)."""
+
+    @staticmethod
+    def normal(shape=(), dtype=float32, loc=0.0, scale=1.0, key=None):
+        return _wrap((np.random.normal(size=shape) * scale + loc).astype(dtype))
 
 
 def where(c, a, b):
