@@ -51,6 +51,7 @@ def parse_args():
     ap.add_argument("--no-multiview", action="store_true",
                     help="skip the C4 render and C3 training measurements that follow the C2 headline")
     ap.add_argument("--mv-steps", type=int, default=2, help="timed steps of each multi-view measurement")
+    ap.add_argument("--streams", type=int, default=2, help="CUDA streams the C4 views are pipelined over")
     ap.add_argument("--sync-allreduce", action="store_true",
                     help="multi-GPU C2: every step waits for its own gradient exchange (no overlap)")
     ap.add_argument("--exchange", choices=["screen", "allreduce"], default="screen",
@@ -616,11 +617,11 @@ def run_multiview(args, world, rank, local, config=None, steps=None, warmup=None
         def step():
             trainer.step_views(cams, targets, total_views=len(scene.cameras))
     else:
+        # views pipelined over two CUDA streams (GaussianModel.render_views);
+        # every output is produced on the device and dropped
         def step():
-            with torch.no_grad():
-                for cam in cams:
-                    out = model.render(cam, antialias=cfg.antialias, render_depth=True)
-                    dups.append(out["n_duplicates"])
+            model.render_views(cams, antialias=cfg.antialias, render_depth=True, streams=args.streams,
+                               on_output=lambda i, out: dups.append(out["n_duplicates"]))
 
     def barrier():
         if world > 1:

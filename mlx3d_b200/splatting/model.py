@@ -21,7 +21,8 @@ import torch
 
 from .. import _native as nat
 from ..cameras import Camera
-from .render import _check_projection, _render_composed, _render_fused, render_gaussian_depth, render_gaussian_features
+from .render import (_check_projection, _render_composed, _render_fused, render_gaussian_depth,
+                     render_gaussian_features, side_streams)
 from .sh import num_sh_bases, rgb_to_sh
 
 __all__ = ["GaussianModel"]
@@ -134,6 +135,37 @@ class GaussianModel:
             flags=nat.GS_ACT_EXP_SCALES | nat.GS_ACT_SIGMOID_OPACITY,
             with_depth=render_depth,
         )
+
+    def render_views(self, cameras, background: torch.Tensor | None = None, antialias: bool = False,
+                     render_depth: bool = False, streams: int = 2, on_output=None) -> list:
+        """Render several views, pipelined over ``streams`` CUDA streams: view
+        i runs on stream i mod ``streams``, so one view's per-Gaussian pass
+        and binning (latency bound, and the host's wait for the duplicate
+        count) overlap another view's compositor.  Forward only (no
+        autograd graph is kept).  ``on_output(i, out)`` is called for every
+        view as soon as its work is enqueued, on that view's stream (as the
+        current stream); its return value is collected instead of the
+        outputs when given (keeping 256 4K outputs alive would need tens of
+        GB).  The current stream waits for all views before this returns."""
+        cur = torch.cuda.current_stream()
+        ss = side_streams(max(1, int(streams)))
+        for s in ss:
+            s.wait_stream(cur)
+        results = []
+        with torch.no_grad():
+            for i, cam in enumerate(cameras):
+                s = ss[i % len(ss)]
+                with torch.cuda.stream(s):
+                    out = self.render(cam, background=background, antialias=antialias, render_depth=render_depth)
+                    results.append(on_output(i, out) if on_output is not None else out)
+        for s in ss:
+            cur.wait_stream(s)
+        if on_output is None:
+            for out in results:  # outputs made on side streams are used on the current one
+                for v in out.values():
+                    if isinstance(v, torch.Tensor) and v.is_cuda:
+                        v.record_stream(cur)
+        return results
 
     def render_depth(self, camera: Camera, antialias: bool = False, projection: str = "ewa") -> dict:
         """Expected depth (model.py:166-180)."""

@@ -189,6 +189,20 @@ _grad_sink = None
 _screen_hook = None
 
 
+_SIDE_STREAMS: dict = {}
+
+
+def side_streams(count: int) -> list:
+    """``count`` CUDA streams of the current device, created once and reused:
+    the caching allocator keeps freed blocks per stream, so fresh streams on
+    every call would never reuse memory (each call would allocate anew)."""
+    dev = torch.cuda.current_device()
+    have = _SIDE_STREAMS.setdefault(dev, [])
+    while len(have) < count:
+        have.append(torch.cuda.Stream(device=dev))
+    return have[:count]
+
+
 def set_screen_grad_hook(fn) -> None:
     global _screen_hook
     _screen_hook = fn

@@ -30,7 +30,7 @@ from ..cameras import Camera
 from ..distributed import allreduce_gradients, world
 from ..losses import l1_dssim_loss
 from .model import GaussianModel
-from .render import _render_fused
+from .render import _render_fused, side_streams
 
 __all__ = ["TrainerConfig", "GaussianTrainer"]
 
@@ -118,21 +118,24 @@ class GaussianTrainer:
         self.grad_count = torch.zeros((n,), dtype=torch.float32, device=dev)
 
     # ------------------------------------------------------------- pieces
-    def _view_loss(self, camera: Camera, target: torch.Tensor, probe: torch.Tensor | None, scale: float):
+    def _view_forward(self, camera: Camera, target: torch.Tensor, probe: torch.Tensor | None):
+        """Render + loss of one view (graph kept for the backward)."""
         cfg = self.config
         dev = self.model.params["means"].device
         bg = torch.ones(3, device=dev) if cfg.white_background else torch.zeros(3, device=dev)
         p = self.model.params
         if cfg.projection == "ut":
             out = self.model.render(camera, background=bg, antialias=cfg.antialias, projection="ut")
-            loss, _, _ = l1_dssim_loss(out["image"], target, cfg.lambda_dssim)
-            (loss * scale).backward()
-            return loss.detach(), out
-        out = _render_fused(
-            camera, p["means"], p["quats"], p["scales"], p["opacities"], sh_dc=p["sh_dc"], sh_rest=p["sh_rest"],
-            sh_degree=self.model.active_sh_degree, background=bg, antialias=cfg.antialias,
-            flags=nat.GS_ACT_EXP_SCALES | nat.GS_ACT_SIGMOID_OPACITY, probe=probe)
+        else:
+            out = _render_fused(
+                camera, p["means"], p["quats"], p["scales"], p["opacities"], sh_dc=p["sh_dc"], sh_rest=p["sh_rest"],
+                sh_degree=self.model.active_sh_degree, background=bg, antialias=cfg.antialias,
+                flags=nat.GS_ACT_EXP_SCALES | nat.GS_ACT_SIGMOID_OPACITY, probe=probe)
         loss, _, _ = l1_dssim_loss(out["image"], target, cfg.lambda_dssim)
+        return loss, out
+
+    def _view_loss(self, camera: Camera, target: torch.Tensor, probe: torch.Tensor | None, scale: float):
+        loss, out = self._view_forward(camera, target, probe)
         (loss * scale).backward()
         return loss.detach(), out
 
@@ -242,8 +245,50 @@ class GaussianTrainer:
         opacity_reset, sh_changed = self._schedules_after_update()
         return self._info(float(loss), opacity_reset, sh_changed, densify)
 
+    def _views_backward(self, cameras, targets, scale: float, streams: int) -> list:
+        """Forward + backward of every view, gradients accumulated in .grad.
+
+        With ``streams`` > 1 the views are pipelined: view i's forward runs
+        on stream i mod ``streams`` while view i-1's backward runs on its own
+        stream, so the latency-bound per-Gaussian pass and binning of one view
+        overlap the compositor backward of the other.  Every backward waits
+        for the previous view's backward (an event), so the accumulations
+        into .grad stay ordered; the current stream waits for all of them.
+        Returns the detached per-view losses (usable on the current stream)."""
+        if streams <= 1 or len(cameras) <= 1:
+            return [self._view_loss(c, t, None, scale)[0] for c, t in zip(cameras, targets)]
+        cur = torch.cuda.current_stream()
+        ss = side_streams(streams)
+        for s in ss:
+            s.wait_stream(cur)
+        losses, prev_bwd, pending = [], None, None
+        for i, (cam, tgt) in enumerate(zip(cameras, targets)):
+            s = ss[i % len(ss)]
+            with torch.cuda.stream(s):
+                loss, _ = self._view_forward(cam, tgt, None)
+            if pending is not None:  # previous view's backward, issued after this view's forward
+                prev_bwd = self._issue_backward(*pending, prev_bwd)
+            pending = (loss, scale, s)
+            losses.append(loss.detach())
+        self._issue_backward(*pending, prev_bwd)
+        for s in ss:
+            cur.wait_stream(s)
+        for loss in losses:  # made on the side streams, read on the current one
+            loss.record_stream(cur)
+        return losses
+
+    @staticmethod
+    def _issue_backward(loss, scale, s, after):
+        with torch.cuda.stream(s):
+            if after is not None:
+                s.wait_event(after)
+            (loss * scale).backward()
+            done = torch.cuda.Event()
+            done.record(s)
+        return done
+
     def step_views(self, cameras: list[Camera], targets: list[torch.Tensor], total_views: int | None = None,
-                   monitor=None) -> dict:
+                   monitor=None, streams: int = 2) -> dict:
         """One data-parallel step over a batch of views: this rank renders
         ``cameras`` (its shard), the loss is averaged over ``total_views``
         (all ranks' views), gradients are summed over ranks (NCCL all-reduce)
@@ -256,10 +301,8 @@ class GaussianTrainer:
         rank, ws = world()
         if total_views is None:
             total_views = len(cameras) * ws
-        loss_sum = torch.zeros((), device=self.model.params["means"].device)
-        for cam, tgt in zip(cameras, targets):
-            loss, _ = self._view_loss(cam, tgt, None, 1.0 / total_views)
-            loss_sum += loss
+        losses = self._views_backward(cameras, targets, 1.0 / total_views, streams)
+        loss_sum = torch.stack(losses).sum() if losses else torch.zeros((), device=self.model.params["means"].device)
         allreduce_gradients({k: self.model.params[k] for k in _GROUPS})
         self._adam()
         self._mcmc_noise()

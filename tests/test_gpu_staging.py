@@ -61,17 +61,23 @@ def test_gradient_sink_writes_render_gradients_into_the_reducer_buffer():
                 loss.backward()
         else:
             loss.backward()
+        ptrs = {k: p.grad.data_ptr() for k, p in params.items()}
+        grads_ = {k: p.grad.clone() for k, p in params.items()}
         red.stage(params)
         flat = red.finish()
-        return params, flat
+        return params, flat, ptrs, grads_
 
-    p1, f1 = grads(True)
-    p2, f2 = grads(False)
+    p1, f1, ptr1, g1 = grads(True)
+    p2, f2, ptr2, g2 = grads(False)
     torch.cuda.synchronize()
-    # with the sink every gradient is a view of the reducer's flat buffer
+    # with the sink every gradient was a view of the reducer's flat buffer ...
     lo, hi = f1.data_ptr(), f1.data_ptr() + f1.numel() * 4
-    assert all(lo <= p.grad.data_ptr() < hi for p in p1.values())
+    assert all(lo <= v < hi for v in ptr1.values())
+    # ... and stage() detached those views from the parameters (the buffer is
+    # reduced in place next); copied gradients stay attached
+    assert all(p.grad is None for p in p1.values())
+    assert all(p.grad is not None for p in p2.values())
     # (atomic accumulation order differs between two backward passes)
     assert float((f1 - f2).norm() / f2.norm()) < 1e-5
     for k in p1:
-        assert float((p1[k].grad - p2[k].grad).norm() / p2[k].grad.norm().clamp_min(1e-30)) < 1e-5, k
+        assert float((g1[k] - g2[k]).norm() / g2[k].norm().clamp_min(1e-30)) < 1e-5, k
