@@ -54,9 +54,11 @@ def parse_args():
     ap.add_argument("--streams", type=int, default=2, help="CUDA streams the C4 views are pipelined over")
     ap.add_argument("--sync-allreduce", action="store_true",
                     help="multi-GPU C2: every step waits for its own gradient exchange (no overlap)")
-    ap.add_argument("--exchange", choices=["screen", "allreduce"], default="screen",
-                    help="multi-GPU C2: all-to-all of the screen-space cotangents + view-batched per-Gaussian "
-                         "backward (reduce-scattered gradient), or an all-reduce of the parameter gradients")
+    ap.add_argument("--exchange", choices=["peer", "screen", "allreduce"], default="peer",
+                    help="multi-GPU C2: screen-space cotangents read from the other GPUs' memory by the "
+                         "view-batched per-Gaussian backward (peer), or exchanged by an NCCL all-to-all first "
+                         "(screen); both leave the summed gradient reduce-scattered.  Or an all-reduce of the "
+                         "parameter gradients (allreduce)")
     return ap.parse_args()
 
 
@@ -212,11 +214,13 @@ def run_ours(args, world, rank, local):
     # (GradientReducer, two flat buffers).  The last one is waited for before
     # the timed region closes.  --sync-allreduce makes every step wait for
     # its own all-reduce instead.
-    from mlx3d_b200.distributed import ScreenGradientExchange
+    from mlx3d_b200.distributed import PeerScreenExchange, ScreenGradientExchange
 
     reducer = GradientReducer()
-    screen = world > 1 and args.exchange == "screen"
-    exchange = ScreenGradientExchange()
+    screen = world > 1 and args.exchange in ("screen", "peer")
+    exchange = PeerScreenExchange() if args.exchange == "peer" else ScreenGradientExchange()
+    if screen and args.exchange == "peer":
+        exchange.prepare(params["means"].shape[0], dev)
     overlap = world > 1 and not screen and not args.sync_allreduce
     # screen exchange: step k's all-to-all runs on NCCL's stream under step
     # k+1's forward; its per-Gaussian backward is launched once step k+1's
@@ -401,6 +405,8 @@ def run_ours(args, world, rank, local):
         e2e = {"value": round(float(te.item()) / world, 4), "unit": "ms/frame", "h2d_bytes_per_step": int(h2d),
                "d2h_bytes_per_step": 4}
 
+    if isinstance(exchange, PeerScreenExchange):
+        exchange.close()  # collective: unmaps the peers' buffers on every rank
     if rank != 0:
         return None
     clk = clocks.summary()
@@ -430,9 +436,14 @@ def run_ours(args, world, rank, local):
             "duplicates": d,
             "visible_gaussians": visible,
             "parallelism": ((f"views sharded over {world} GPU(s); screen-space cotangents (9 floats per "
-                             f"Gaussian) exchanged by one NCCL all-to-all per step, then one view-batched "
-                             f"per-Gaussian backward per rank over its 1/{world} of the Gaussians: the summed "
-                             f"gradient ends reduce-scattered across ranks")
+                             f"Gaussian) "
+                             + ("read by each rank's view-batched per-Gaussian backward straight from the other "
+                                "GPUs' memory (CUDA IPC mappings, peer loads over NVLink; one 1-float NCCL "
+                                "all-reduce per step as the barrier)" if args.exchange == "peer" else
+                                "exchanged by one NCCL all-to-all per step, then one view-batched per-Gaussian "
+                                "backward per rank")
+                             + f" over its 1/{world} of the Gaussians: the summed gradient ends reduce-scattered "
+                               f"across ranks")
                             if screen else
                             (f"views sharded over {world} GPU(s); per-Gaussian gradient all-reduce (NCCL, one "
                              f"flat 59-float-per-Gaussian buffer per step, "

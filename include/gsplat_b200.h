@@ -181,6 +181,34 @@ int gs_preprocess_backward_views(const gs_camera* cams, int n_views, const float
                                  float* g_quats, float* g_scales, float* g_opacities, float* g_sh_dc,
                                  float* g_sh_rest, void* stream);
 
+/* gs_preprocess_backward_views with the cotangents of each view given as
+ * four arrays instead of packed rows: cotangents is a DEVICE array of
+ * 4 * n_views pointers, for view v: dL/d means2d (n,2), conic (n,3), colour
+ * (n,3) and effective opacity (n) of Gaussian 0 of the slice.  The arrays
+ * may live in other GPUs' memory (mapped with gs_peer_open): the kernel
+ * reads them with peer loads over NVLink, so a rank reduces its slice of
+ * every rank's cotangents without an all-to-all.  No reference
+ * counterpart (see gs_preprocess_backward_views). */
+int gs_preprocess_backward_views_peer(const gs_camera* cams, int n_views, const float* means,
+                                      const float* quats, const float* scales, const float* opacities,
+                                      const float* sh_dc, int64_t sh_dc_stride, const float* sh_rest,
+                                      int64_t sh_rest_stride, int sh_degree, int64_t n, float blur,
+                                      int antialias, int flags, const float* const* cotangents, float* g_means,
+                                      float* g_quats, float* g_scales, float* g_opacities, float* g_sh_dc,
+                                      float* g_sh_rest, void* stream);
+
+/* Device buffers shared between the processes of one node (CUDA IPC; no
+ * reference counterpart: mlx3D is single-device).  gs_peer_alloc allocates
+ * `bytes` of device memory on the current device and writes its 64-byte
+ * handle; another process maps it with gs_peer_open (its GPU must be able to
+ * reach this one: NVLink / NVSwitch peers) and unmaps it with gs_peer_close
+ * before the owner calls gs_peer_free. */
+#define GS_PEER_HANDLE_BYTES 64
+int gs_peer_alloc(size_t bytes, void** dev_ptr, void* handle);
+int gs_peer_open(const void* handle, void** dev_ptr);
+int gs_peer_close(void* dev_ptr);
+int gs_peer_free(void* dev_ptr);
+
 /* ------------------------------------------------------------------- binning
  * bin_gaussians (src/mlx3d/splatting/tiles.py:19-182), split where the
  * reference itself synchronises with the host (tiles.py:68):

@@ -100,6 +100,16 @@ _SIGS = {
         + [_P] * 6
         + [_P],
     ),
+    "gs_preprocess_backward_views_peer": (
+        c_int,
+        [_P, c_int, _P, _P, _P, _P, _P, c_int64, _P, c_int64, c_int, c_int64, c_float, c_int, c_int, _P]
+        + [_P] * 6
+        + [_P],
+    ),
+    "gs_peer_alloc": (c_int, [c_size_t, ctypes.POINTER(c_void_p), _P]),
+    "gs_peer_open": (c_int, [_P, ctypes.POINTER(c_void_p)]),
+    "gs_peer_close": (c_int, [_P]),
+    "gs_peer_free": (c_int, [_P]),
     "gs_tile_counts": (c_int, [_P, _P, c_int64, c_int, c_int, _P, _P]),
     "gs_bin_workspace_n_bytes": (c_size_t, [c_int64]),
     "gs_bin_workspace_d_bytes": (c_size_t, [c_int64]),
@@ -205,3 +215,18 @@ def require_cuda(name: str, t: torch.Tensor, dtype=torch.float32) -> torch.Tenso
     if t.dtype != dtype:
         t = t.to(dtype)
     return t.contiguous()
+
+
+class _CudaArray:
+    """Minimal __cuda_array_interface__ exporter for a raw device pointer."""
+
+    def __init__(self, ptr: int, shape: tuple, typestr: str):
+        self.__cuda_array_interface__ = {"shape": tuple(int(d) for d in shape), "typestr": typestr,
+                                         "data": (int(ptr), False), "version": 3, "strides": None}
+
+
+def wrap_device(ptr: int, shape: tuple, device, dtype=torch.float32) -> torch.Tensor:
+    """A tensor aliasing device memory this library allocated (no copy; the
+    memory must outlive the tensor)."""
+    typestr = {torch.float32: "<f4", torch.int32: "<i4", torch.int64: "<i8", torch.uint8: "|u1"}[dtype]
+    return torch.as_tensor(_CudaArray(ptr, shape, typestr), device=device)

@@ -601,11 +601,14 @@ struct PreBwdViewsArgs {
   PreFwdArgs f;                // cam unused
   const gs_camera* cams;       // device array of n_views cameras
   int n_views;
-  const float* g_screen;       // view v, Gaussian i: g_screen + v * view_stride + 9 i
+  const float* g_screen;       // packed: view v, Gaussian i at g_screen + v * view_stride + 9 i
   int64_t view_stride;
+  const float* const* cot;     // or per view v: cot[4 v + 0..3] = dL/d means2d (2), conic (3),
+                               // colour (3), effective opacity (1) arrays of Gaussian 0 of the slice
   float *g_means, *g_quats, *g_scales, *g_opac, *g_sh_dc, *g_sh_rest;
 };
 
+template <bool PTRS>
 __global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd_views(const PreBwdViewsArgs g) {
   extern __shared__ __align__(16) float smem[];
   const PreFwdArgs& a = g.f;
@@ -655,10 +658,24 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd_views(const PreBwd
     float gm[3] = {0.f, 0.f, 0.f}, gq[4] = {0.f, 0.f, 0.f, 0.f}, gsc[3] = {0.f, 0.f, 0.f}, go = 0.f;
     for (int v = 0; v < g.n_views; ++v) {
       const gs_camera& cam = g.cams[v];
-      const float* cot = g.g_screen + v * g.view_stride + 9 * (int64_t)i;
-      const float gu = __ldg(cot + 0), gv = __ldg(cot + 1);
-      const float gA = __ldg(cot + 2), gB = __ldg(cot + 3), gC = __ldg(cot + 4);
-      const float goo = __ldg(cot + 8);
+      float gu, gv, gA, gB, gC, gcv[3], goo;
+      if (PTRS) {
+        // cotangents of view v: possibly another GPU's memory (peer loads)
+        const float* const* t = g.cot + 4 * v;
+        const float* pm = t[0] + 2 * (int64_t)i;
+        const float* pc = t[1] + 3 * (int64_t)i;
+        const float* pk = t[2] + 3 * (int64_t)i;
+        gu = pm[0]; gv = pm[1];
+        gA = pc[0]; gB = pc[1]; gC = pc[2];
+        gcv[0] = pk[0]; gcv[1] = pk[1]; gcv[2] = pk[2];
+        goo = t[3][i];
+      } else {
+        const float* cot = g.g_screen + v * g.view_stride + 9 * (int64_t)i;
+        gu = __ldg(cot + 0); gv = __ldg(cot + 1);
+        gA = __ldg(cot + 2); gB = __ldg(cot + 3); gC = __ldg(cot + 4);
+        gcv[0] = __ldg(cot + 5); gcv[1] = __ldg(cot + 6); gcv[2] = __ldg(cot + 7);
+        goo = __ldg(cot + 8);
+      }
       // opacities_out = act(opacity) * compensation   (render.py:75)
       Proj p;
       project_one(cam, m0, m1, m2, q.x, q.y, q.z, q.w, s0, s1, s2, a.blur, a.aa != 0, p);
@@ -683,7 +700,7 @@ __global__ void __launch_bounds__(kPreBlock) k_preprocess_bwd_views(const PreBwd
           float r = gs_mul(bs[0], s_dc[li * dld + ch]);
           for (int k = 1; k < nb; ++k) r = gs_add(r, gs_mul(bs[k], s_rest[li * rest_ld + (k - 1) * 3 + ch]));
           r = gs_add(r, 0.5f);
-          const float gcol = r > 0.0f ? __ldg(cot + 5 + ch) : 0.0f;
+          const float gcol = r > 0.0f ? gcv[ch] : 0.0f;
           s_g[li * kViewsGradPitch + ch] += bs[0] * gcol;
           for (int k = 1; k < nb; ++k) s_g[li * kViewsGradPitch + 3 + (k - 1) * 3 + ch] += bs[k] * gcol;
         }
@@ -919,22 +936,20 @@ int gs_preprocess_backward(const gs_camera* cam, const float* means, const float
   return check_launch("k_preprocess_bwd");
 }
 
-int gs_preprocess_backward_views(const gs_camera* cams, int n_views, const float* means,
-                                 const float* quats, const float* scales, const float* opacities,
-                                 const float* sh_dc, int64_t sh_dc_stride, const float* sh_rest,
-                                 int64_t sh_rest_stride, int sh_degree, int64_t n, float blur, int antialias,
-                                 int flags, const float* g_screen, int64_t view_stride, float* g_means,
-                                 float* g_quats, float* g_scales, float* g_opacities, float* g_sh_dc,
-                                 float* g_sh_rest, void* stream) {
-  clear_error();
+static int views_bwd_impl(const gs_camera* cams, int n_views, const float* means, const float* quats,
+                          const float* scales, const float* opacities, const float* sh_dc, int64_t sh_dc_stride,
+                          const float* sh_rest, int64_t sh_rest_stride, int sh_degree, int64_t n, float blur,
+                          int antialias, int flags, const float* g_screen, int64_t view_stride,
+                          const float* const* cot, float* g_means, float* g_quats, float* g_scales,
+                          float* g_opacities, float* g_sh_dc, float* g_sh_rest, void* stream) {
   if (n < 0) return set_error(GS_ERR_INVALID_ARG, "n must be >= 0");
   if (n_views < 0) return set_error(GS_ERR_INVALID_ARG, "n_views must be >= 0");
   if (n == 0) return GS_OK;
   if (!cams && n_views > 0) return set_error(GS_ERR_INVALID_ARG, "cams is NULL");
   if (!means || !quats || !scales || !opacities || !g_means || !g_quats || !g_scales || !g_opacities ||
-      (n_views > 0 && !g_screen))
+      (n_views > 0 && !g_screen && !cot))
     return set_error(GS_ERR_INVALID_ARG, "gs_preprocess_backward_views: NULL pointer");
-  if (view_stride < 9 * n && n_views > 1)
+  if (!cot && view_stride < 9 * n && n_views > 1)
     return set_error(GS_ERR_INVALID_ARG, "view_stride %lld is below 9 n = %lld", (long long)view_stride,
                      (long long)(9 * n));
   if (!aligned(quats, 16) || !aligned(g_quats, 16))
@@ -949,17 +964,47 @@ int gs_preprocess_backward_views(const gs_camera* cams, int n_views, const float
   a.means = means; a.quats = quats; a.scales = scales; a.opac = opacities;
   a.sh_dc = sh_dc; a.sh_rest = sh_rest; a.dc_stride = sh_dc_stride; a.rest_stride = sh_rest_stride;
   a.sh_degree = deg; a.n = n; a.blur = blur; a.aa = antialias && blur > 0.0f; a.flags = flags; a.fused = 1;
-  g.cams = cams; g.n_views = n_views; g.g_screen = g_screen; g.view_stride = view_stride;
+  g.cams = cams; g.n_views = n_views; g.g_screen = g_screen; g.view_stride = view_stride; g.cot = cot;
   g.g_means = g_means; g.g_quats = g_quats; g.g_scales = g_scales; g.g_opac = g_opacities;
   g.g_sh_dc = g_sh_dc; g.g_sh_rest = g_sh_rest;
   const size_t sm = pre_smem_bytes(deg, true) + (deg >= 0 ? sizeof(float) * kPreBlock * kViewsGradPitch : 0);
+  auto kern = cot ? k_preprocess_bwd_views<true> : k_preprocess_bwd_views<false>;
   if (sm > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(k_preprocess_bwd_views, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                         (int)sm);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) return set_error(GS_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
   }
-  k_preprocess_bwd_views<<<(unsigned)ceil_div(n, kPreBlock), kPreBlock, sm, as_stream(stream)>>>(g);
+  kern<<<(unsigned)ceil_div(n, kPreBlock), kPreBlock, sm, as_stream(stream)>>>(g);
   return check_launch("k_preprocess_bwd_views");
+}
+
+int gs_preprocess_backward_views(const gs_camera* cams, int n_views, const float* means,
+                                 const float* quats, const float* scales, const float* opacities,
+                                 const float* sh_dc, int64_t sh_dc_stride, const float* sh_rest,
+                                 int64_t sh_rest_stride, int sh_degree, int64_t n, float blur, int antialias,
+                                 int flags, const float* g_screen, int64_t view_stride, float* g_means,
+                                 float* g_quats, float* g_scales, float* g_opacities, float* g_sh_dc,
+                                 float* g_sh_rest, void* stream) {
+  clear_error();
+  if (!g_screen && n_views > 0 && n > 0)
+    return set_error(GS_ERR_INVALID_ARG, "gs_preprocess_backward_views: g_screen is NULL");
+  return views_bwd_impl(cams, n_views, means, quats, scales, opacities, sh_dc, sh_dc_stride, sh_rest,
+                        sh_rest_stride, sh_degree, n, blur, antialias, flags, g_screen, view_stride, nullptr,
+                        g_means, g_quats, g_scales, g_opacities, g_sh_dc, g_sh_rest, stream);
+}
+
+int gs_preprocess_backward_views_peer(const gs_camera* cams, int n_views, const float* means,
+                                      const float* quats, const float* scales, const float* opacities,
+                                      const float* sh_dc, int64_t sh_dc_stride, const float* sh_rest,
+                                      int64_t sh_rest_stride, int sh_degree, int64_t n, float blur,
+                                      int antialias, int flags, const float* const* cotangents, float* g_means,
+                                      float* g_quats, float* g_scales, float* g_opacities, float* g_sh_dc,
+                                      float* g_sh_rest, void* stream) {
+  clear_error();
+  if (!cotangents && n_views > 0 && n > 0)
+    return set_error(GS_ERR_INVALID_ARG, "gs_preprocess_backward_views_peer: cotangents is NULL");
+  return views_bwd_impl(cams, n_views, means, quats, scales, opacities, sh_dc, sh_dc_stride, sh_rest,
+                        sh_rest_stride, sh_degree, n, blur, antialias, flags, nullptr, 0, cotangents, g_means,
+                        g_quats, g_scales, g_opacities, g_sh_dc, g_sh_rest, stream);
 }
 
 int gs_eval_sh_forward(int degree, const float* sh, int64_t n, int k, int channels,

@@ -15,8 +15,8 @@ import time
 import torch
 import torch.distributed as dist
 
-__all__ = ["shard_views", "allreduce_gradients", "GradientReducer", "ScreenGradientExchange", "PeerLost",
-           "PeerMonitor", "world"]
+__all__ = ["shard_views", "allreduce_gradients", "GradientReducer", "ScreenGradientExchange",
+           "PeerScreenExchange", "PeerLost", "PeerMonitor", "world"]
 
 
 def world() -> tuple[int, int]:
@@ -278,7 +278,6 @@ class ScreenGradientExchange:
         hi), "means", "quats", "scales", "opacities", "sh_a", "sh_b"}
         (gradient slices; sh_b is None at SH degree 0)."""
         from . import _native as nat
-        from .splatting.render import _sh_layout
 
         if not self._pending:
             raise RuntimeError("ScreenGradientExchange: nothing in flight")
@@ -291,13 +290,35 @@ class ScreenGradientExchange:
         dev = means.device
         lo, hi = self.slice_of(n, e["rank"], ws)
         m = hi - lo
-        f32 = dict(device=dev, dtype=torch.float32)
-        out = {"range": (lo, hi), "means": torch.empty((m, 3), **f32), "quats": torch.empty((m, 4), **f32),
-               "scales": torch.empty((m, 3), **f32), "opacities": torch.empty((m,), **f32),
-               "sh_a": torch.empty((m,) + tuple(sh_a.shape[1:]), **f32),
-               "sh_b": None if sh_b is None else torch.empty((m,) + tuple(sh_b.shape[1:]), **f32)}
+        out = self._alloc_out(m, sh_a, sh_b, dev)
+        out["range"] = (lo, hi)
         if m == 0:
             return out
+        dc, dcs, rest, rests, g_dc, g_rest = self._sh_pointers(cfg, sh_a, sh_b, out)
+        off = lambda p, stride: None if p is None else p + 4 * lo * stride  # noqa: E731
+        nat.call(
+            "gs_preprocess_backward_views", e["cams"].data_ptr(), ws, nat.ptr(means[lo:hi]),
+            nat.ptr(quats[lo:hi]), nat.ptr(scales[lo:hi]), nat.ptr(opac[lo:hi]), off(dc, dcs), dcs,
+            off(rest, rests), rests, cfg.sh_degree, m, cfg.blur, int(cfg.antialias), cfg.flags,
+            e["recv"].data_ptr(), per * 9, nat.ptr(out["means"]), nat.ptr(out["quats"]), nat.ptr(out["scales"]),
+            nat.ptr(out["opacities"]), g_dc, g_rest, nat.stream(),
+        )
+        return out
+
+    @staticmethod
+    def _alloc_out(m, sh_a, sh_b, dev) -> dict:
+        f32 = dict(device=dev, dtype=torch.float32)
+        return {"means": torch.empty((m, 3), **f32), "quats": torch.empty((m, 4), **f32),
+                "scales": torch.empty((m, 3), **f32), "opacities": torch.empty((m,), **f32),
+                "sh_a": torch.empty((m,) + tuple(sh_a.shape[1:]), **f32),
+                "sh_b": None if sh_b is None else torch.empty((m,) + tuple(sh_b.shape[1:]), **f32)}
+
+    @staticmethod
+    def _sh_pointers(cfg, sh_a, sh_b, out):
+        """Input SH layout and the gradient pointers of ``out`` (zeroing
+        coefficient rows beyond the active degree, which are not written)."""
+        from .splatting.render import _sh_layout
+
         dc, dcs, rest, rests = _sh_layout(cfg, sh_a, sh_b)
         g_dc = out["sh_a"].data_ptr()
         g_rest = None
@@ -309,20 +330,192 @@ class ScreenGradientExchange:
             g_rest = out["sh_b"].data_ptr()
             if sh_b.shape[1] + 1 > (cfg.sh_degree + 1) ** 2:
                 out["sh_b"].zero_()
-        off = lambda p, stride: None if p is None else p + 4 * lo * stride  # noqa: E731
-        nat.call(
-            "gs_preprocess_backward_views", e["cams"].data_ptr(), ws, nat.ptr(means[lo:hi]),
-            nat.ptr(quats[lo:hi]), nat.ptr(scales[lo:hi]), nat.ptr(opac[lo:hi]), off(dc, dcs), dcs,
-            off(rest, rests), rests, cfg.sh_degree, m, cfg.blur, int(cfg.antialias), cfg.flags,
-            e["recv"].data_ptr(), per * 9, nat.ptr(out["means"]), nat.ptr(out["quats"]), nat.ptr(out["scales"]),
-            nat.ptr(out["opacities"]), g_dc, g_rest, nat.stream(),
-        )
-        return out
+        return dc, dcs, rest, rests, g_dc, g_rest
 
     def reduce(self) -> dict:
         """start() + finish() of the captured backward."""
         self.start()
         return self.finish()
+
+
+class PeerScreenExchange(ScreenGradientExchange):
+    """:class:`ScreenGradientExchange` without the all-to-all: the compositor
+    backward of every rank writes its cotangents into a device buffer that
+    the other GPUs of the node have mapped (CUDA IPC, ``gs_peer_*``), and
+    rank r's view-batched backward (``gs_preprocess_backward_views_peer``)
+    reads its slice of every rank's cotangents with peer loads over NVLink.
+    The only collective left is a one-float NCCL all-reduce per step used as
+    a stream-ordered barrier: when it completes, every rank's cotangents of
+    that step are written.  Two buffer slots alternate, so a rank writes step
+    k + 2 into the slot of step k only after the barrier of step k + 1,
+    which every rank reaches after its backward of step k has read it.
+
+    Same usage and result as :class:`ScreenGradientExchange`; needs every
+    rank's GPU to reach the others' memory (one NVLink / NVSwitch node).
+    Call :meth:`close` on every rank before the process group is destroyed."""
+
+    def __init__(self, group=None):
+        super().__init__(group)
+        self._n = None
+        self._own = None
+        self._mapped = []
+        self._tables = None
+        self._local = None
+        self._flag = None
+        self._slot_next = 0
+        self._dest_slot = None
+
+    @staticmethod
+    def _layout(n):
+        """Byte offsets of the four arrays of one slot (16-byte aligned) and the slot size."""
+        a16 = lambda b: (b + 15) & ~15  # noqa: E731
+        o_m2d = 0
+        o_con = a16(o_m2d + 8 * n)
+        o_col = a16(o_con + 12 * n)
+        o_op = a16(o_col + 12 * n)
+        return (o_m2d, o_con, o_col, o_op), a16(o_op + 4 * n)
+
+    def _setup(self, n: int, dev) -> None:
+        import ctypes
+
+        from . import _native as nat
+
+        if self._n == n and self._own is not None:
+            return
+        self.close()
+        rank, ws = world()
+        offs, slot_bytes = self._layout(n)
+        ptr = ctypes.c_void_p()
+        handle = (ctypes.c_char * 64)()
+        nat.call("gs_peer_alloc", 2 * slot_bytes, ctypes.byref(ptr), handle)
+        self._own = ptr.value
+        handles = [bytes(handle)] * ws
+        if ws > 1:
+            dist.all_gather_object(handles, bytes(handle), group=self.group)
+        bases = []
+        for r in range(ws):
+            if r == rank:
+                bases.append(self._own)
+                continue
+            p = ctypes.c_void_p()
+            nat.call("gs_peer_open", handles[r], ctypes.byref(p))
+            self._mapped.append(p.value)
+            bases.append(p.value)
+        lo, hi = self.slice_of(n, rank, ws)
+        self._tables, self._local = [], []
+        for sl in range(2):
+            ptrs = []
+            for r in range(ws):
+                b = bases[r] + sl * slot_bytes
+                ptrs += [b + offs[0] + 8 * lo, b + offs[1] + 12 * lo, b + offs[2] + 12 * lo, b + offs[3] + 4 * lo]
+            self._tables.append(torch.tensor(ptrs, dtype=torch.int64, device=dev))
+            b = self._own + sl * slot_bytes
+            self._local.append((nat.wrap_device(b + offs[0], (n, 2), dev), nat.wrap_device(b + offs[1], (n, 3), dev),
+                                nat.wrap_device(b + offs[2], (n, 3), dev), nat.wrap_device(b + offs[3], (n,), dev)))
+        self._flag = torch.zeros((1,), device=dev)
+        self._n = n
+
+    def prepare(self, n: int, device) -> None:
+        """Allocate and map the shared buffers for ``n`` Gaussians now
+        (collective: every rank calls it).  Otherwise the first backward does
+        it, from autograd's thread; call this first in code that times
+        steps or mixes other collectives."""
+        self._setup(int(n), torch.device(device))
+
+    @contextlib.contextmanager
+    def capture(self):
+        from .splatting import render as _render
+
+        def hook(cfg, cot, params):
+            self._captured = (cfg, cot, params, self._dest_slot)
+            self._dest_slot = None
+
+        def dest(n, dev):
+            self._setup(n, dev)
+            self._dest_slot = self._slot_next
+            self._slot_next ^= 1
+            return self._local[self._dest_slot]
+
+        _render.set_screen_grad_hook(hook, dest)
+        try:
+            yield self
+        finally:
+            _render.set_screen_grad_hook(None)
+
+    def start(self) -> None:
+        if self._captured is None:
+            raise RuntimeError("PeerScreenExchange: no backward was captured")
+        if len(self._pending) >= 2:
+            raise RuntimeError("PeerScreenExchange: two exchanges in flight; finish() one first")
+        cfg, _, params, slot = self._captured
+        self._captured = None
+        if slot is None:
+            raise RuntimeError("PeerScreenExchange: the backward did not write into the shared buffer")
+        rank, ws = world()
+        dev = params[0].device
+        raw = torch.frombuffer(bytearray(bytes(cfg.cam)), dtype=torch.uint8)
+        cam_bytes = raw.pin_memory().to(dev, non_blocking=True)
+        works = []
+        if ws > 1:
+            # the barrier: completes once every rank's compositor backward of this step has written
+            works.append(dist.all_reduce(self._flag, group=self.group, async_op=True))
+            cams = torch.empty((ws * cam_bytes.numel(),), device=dev, dtype=torch.uint8)
+            works.append(dist.all_gather_into_tensor(cams, cam_bytes, group=self.group, async_op=True))
+        else:
+            cams = cam_bytes
+        self._pending.append({"cfg": cfg, "params": params, "slot": slot, "cams": cams, "works": works, "ws": ws,
+                              "rank": rank})
+
+    def finish(self) -> dict:
+        from . import _native as nat
+
+        if not self._pending:
+            raise RuntimeError("PeerScreenExchange: nothing in flight")
+        e = self._pending.pop(0)
+        for w in e["works"]:
+            w.wait()
+        cfg = e["cfg"]
+        means, quats, scales, opac, sh_a, sh_b = e["params"]
+        n, ws = means.shape[0], e["ws"]
+        dev = means.device
+        lo, hi = self.slice_of(n, e["rank"], ws)
+        m = hi - lo
+        out = self._alloc_out(m, sh_a, sh_b, dev)
+        out["range"] = (lo, hi)
+        if m == 0:
+            return out
+        dc, dcs, rest, rests, g_dc, g_rest = self._sh_pointers(cfg, sh_a, sh_b, out)
+        off = lambda p, stride: None if p is None else p + 4 * lo * stride  # noqa: E731
+        nat.call(
+            "gs_preprocess_backward_views_peer", e["cams"].data_ptr(), ws, nat.ptr(means[lo:hi]),
+            nat.ptr(quats[lo:hi]), nat.ptr(scales[lo:hi]), nat.ptr(opac[lo:hi]), off(dc, dcs), dcs,
+            off(rest, rests), rests, cfg.sh_degree, m, cfg.blur, int(cfg.antialias), cfg.flags,
+            self._tables[e["slot"]].data_ptr(), nat.ptr(out["means"]), nat.ptr(out["quats"]),
+            nat.ptr(out["scales"]), nat.ptr(out["opacities"]), g_dc, g_rest, nat.stream(),
+        )
+        return out
+
+    def close(self) -> None:
+        """Unmap the peers' buffers and free this rank's (collective: every
+        rank calls it; waits for this device's work first)."""
+        from . import _native as nat
+
+        if self._own is None:
+            return
+        rank, ws = world()
+        torch.cuda.synchronize()
+        if ws > 1:
+            dist.barrier(group=self.group)
+        for p in self._mapped:
+            nat.call("gs_peer_close", p)
+        self._mapped = []
+        if ws > 1:
+            dist.barrier(group=self.group)
+        self._local = None
+        self._tables = None
+        nat.call("gs_peer_free", self._own)
+        self._own = None
+        self._n = None
 
 
 class PeerLost(RuntimeError):

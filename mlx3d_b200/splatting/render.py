@@ -117,10 +117,16 @@ class _Render(torch.autograd.Function):
         s = nat.stream()
         if g_image is None:
             g_image = torch.zeros((H, W, 3), device=dev, dtype=torch.float32)
-        g_m2d = torch.empty_like(means2d)
-        g_con = torch.empty_like(conics)
-        g_col = torch.empty((n, 3), device=dev, dtype=torch.float32)
-        g_op = torch.empty_like(opac_out)
+        dest = None
+        if _screen_hook is not None and _screen_dest is not None and cfg.sh_mode != "colors":
+            dest = _screen_dest(n, dev)
+        if dest is not None:  # the compositor backward writes where the consumer wants its cotangents
+            g_m2d, g_con, g_col, g_op = dest
+        else:
+            g_m2d = torch.empty_like(means2d)
+            g_con = torch.empty_like(conics)
+            g_col = torch.empty((n, 3), device=dev, dtype=torch.float32)
+            g_op = torch.empty_like(opac_out)
         nat.call(
             "gs_rasterize_backward", nat.ptr(means2d), nat.ptr(conics), nat.ptr(col), 3, nat.ptr(opac_out), n,
             nat.ptr(ids), nat.ptr(ranges), nat.ptr(bg), W, H, tiles_x, tiles_y, nat.ptr(final_T), nat.ptr(n_contrib),
@@ -187,6 +193,11 @@ _grad_sink = None
 # mlx3d_b200.distributed.ScreenGradientExchange) runs the per-Gaussian
 # backward itself.  Module global for the same reason as _grad_sink.
 _screen_hook = None
+# With the hook, optionally: a callable (n, device) -> (g_means2d (n,2),
+# g_conics (n,3), g_colors (n,3), g_opacities_out (n,)) tensors the
+# compositor backward writes its cotangents into (e.g. buffers that other
+# GPUs read directly), or None for fresh ones.
+_screen_dest = None
 
 
 _SIDE_STREAMS: dict = {}
@@ -203,9 +214,10 @@ def side_streams(count: int) -> list:
     return have[:count]
 
 
-def set_screen_grad_hook(fn) -> None:
-    global _screen_hook
+def set_screen_grad_hook(fn, dest=None) -> None:
+    global _screen_hook, _screen_dest
     _screen_hook = fn
+    _screen_dest = dest if fn is not None else None
 
 
 def set_grad_sink(fn) -> None:

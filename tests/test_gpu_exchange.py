@@ -100,3 +100,32 @@ def test_exchange_on_one_rank_equals_ordinary_backward():
                   ("sh_dc", "sh_a"), ("sh_rest", "sh_b")):
         err = rel_l2(got[gk].cpu().numpy(), ref[k].cpu().numpy())
         assert err < TOL, (k, err)
+
+
+def test_peer_exchange_on_one_rank_equals_ordinary_backward():
+    """The peer-memory variant (compositor backward writing into a CUDA IPC
+    buffer, the view-batched backward reading it through a pointer table)
+    on one rank: same gradients as the ordinary backward."""
+    from mlx3d_b200.distributed import PeerScreenExchange
+
+    model, cams, aa = _model(n=20_000, aa=True)
+    for p in model.params.values():
+        p.grad = None
+    _view_loss(model, cams[2], aa, 9).backward()
+    ref = {k: p.grad.clone() for k, p in model.params.items()}
+    for p in model.params.values():
+        p.grad = None
+    ex = PeerScreenExchange()
+    ex.prepare(20_000, "cuda")
+    try:
+        for _ in range(3):  # both buffer slots, then the first again
+            with ex.capture():
+                _view_loss(model, cams[2], aa, 9).backward()
+            got = ex.reduce()
+            torch.cuda.synchronize()
+            for k, gk in (("means", "means"), ("quats", "quats"), ("scales", "scales"), ("opacities", "opacities"),
+                          ("sh_dc", "sh_a"), ("sh_rest", "sh_b")):
+                err = rel_l2(got[gk].cpu().numpy(), ref[k].cpu().numpy())
+                assert err < TOL, (k, err)
+    finally:
+        ex.close()
