@@ -151,6 +151,45 @@ class Camera:
         return (x * radial + 2.0 * p1 * x * y + p2 * (r2 + 2.0 * x * x),
                 y * radial + p1 * (r2 + 2.0 * y * y) + 2.0 * p2 * x * y)
 
+    def _undistort(self, x: torch.Tensor, y: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+        """Inverse lens distortion by eight fixed-point iterations
+        (cameras.py:53-66 Brown-Conrady, :79-91 fisheye); identity without
+        distortion."""
+        c = self.distortion
+        if c is None:
+            return x, y
+        if self.fisheye:
+            k1, k2, k3, k4 = (list(c) + [0.0, 0.0, 0.0, 0.0])[:4]
+            thd = torch.sqrt(x * x + y * y)
+            th = thd
+            for _ in range(8):
+                th2 = th * th
+                th = thd / (1.0 + th2 * (k1 + th2 * (k2 + th2 * (k3 + th2 * k4))))
+            sc = torch.tan(th) / torch.clamp(thd, min=1e-9)
+            return x * sc, y * sc
+        k1, k2, p1, p2 = c[0], c[1], c[2], c[3]
+        k3 = c[4] if len(c) > 4 else 0.0
+        xu, yu = x, y
+        for _ in range(8):
+            r2 = xu * xu + yu * yu
+            radial = 1.0 + r2 * (k1 + r2 * (k2 + r2 * k3))
+            dx = 2.0 * p1 * xu * yu + p2 * (r2 + 2.0 * xu * xu)
+            dy = p1 * (r2 + 2.0 * yu * yu) + 2.0 * p2 * xu * yu
+            xu = (x - dx) / radial
+            yu = (y - dy) / radial
+        return xu, yu
+
+    def unproject_points(self, xy: torch.Tensor, depth: torch.Tensor) -> torch.Tensor:
+        """Pixel coordinates (..., 2) with camera-frame z depths (...,) back to
+        world points (..., 3) (cameras.py:327-336); differentiable torch
+        operations."""
+        xd = (xy[..., 0] - self.cx) / self.fx
+        yd = (xy[..., 1] - self.cy) / self.fy
+        if self.orthographic:
+            return self.camera_to_world(torch.stack([xd, yd, depth], dim=-1))
+        x, y = self._undistort(xd, yd)
+        return self.camera_to_world(torch.stack([x * depth, y * depth, depth], dim=-1))
+
     def lens_native(self) -> GsLens:
         """Lens model of this camera for the unscented projection."""
         lens = GsLens()

@@ -205,6 +205,53 @@ class GaussianModel:
         model.active_sh_degree = degree
         return model
 
+    def apply_2dgs_constraints(self, max_thickness: float) -> None:
+        """Clamp the third local log-scale to log(max_thickness), turning each
+        Gaussian into an oriented disk (2DGS surfels; model.py:128-143)."""
+        thickness = max(float(max_thickness), 1e-8)
+        lim = math.log(thickness)
+        with torch.no_grad():
+            s = self.params["scales"]
+            s[:, 2:3].clamp_(max=lim)
+
+    def surfel_points(self, min_opacity: float = 0.01, max_points: int | None = None,
+                      orient_towards=None) -> tuple[torch.Tensor, torch.Tensor]:
+        """Surfel centres and unit normals (the local z axis) of the Gaussians
+        with activated opacity >= ``min_opacity`` (model.py:210-254).  At
+        most ``max_points`` are kept, ranked by opacity * scale_x * scale_y
+        (the row of largest importance survives when none passes the opacity
+        test); rows keep index order.  ``orient_towards`` flips each normal to
+        face that point."""
+        from .projection import quat_to_rotmat
+
+        if max_points is not None and max_points <= 0:
+            raise ValueError("max_points must be positive when provided.")
+        n = self.num_gaussians
+        dev = self.params["means"].device
+        if n == 0:
+            empty = torch.zeros((0, 3), device=dev)
+            return empty, empty
+        with torch.no_grad():
+            opacity = self.opacities_act
+            scales = self.scales_act
+            importance = opacity * scales[:, 0] * scales[:, 1]
+            keep = opacity >= float(min_opacity)
+            if not bool(keep.any()):
+                keep[int(torch.argmax(importance))] = True
+            keep_idx = torch.nonzero(keep).flatten()
+            if max_points is not None and keep_idx.numel() > max_points:
+                local = torch.topk(importance[keep_idx], max_points).indices
+                keep_idx = keep_idx[local]
+            keep_idx = torch.sort(keep_idx).values
+            points = self.params["means"][keep_idx].clone()
+            normals = quat_to_rotmat(self.params["quats"][keep_idx])[:, :, 2]
+            normals = normals / torch.clamp(torch.linalg.norm(normals, dim=-1, keepdim=True), min=1e-8)
+            if orient_towards is not None:
+                target = torch.as_tensor(orient_towards, dtype=points.dtype, device=dev)
+                flip = ((target - points) * normals).sum(-1, keepdim=True) < 0
+                normals = torch.where(flip, -normals, normals)
+        return points, normals
+
     def one_up_sh_degree(self) -> None:
         if self.active_sh_degree < self.sh_degree:
             self.active_sh_degree += 1

@@ -14,8 +14,11 @@ Screen-space positional gradient norms are accumulated for densification
 model's adaptive density control runs (clone / split / prune, or MCMC
 relocation with ``method="mcmc"``, trainer.py:366-400) and the Adam moments
 follow the surviving rows (new rows start at zero).  The opacity reset and
-SH-degree schedule run as in the reference.  The 2DGS surfel method is not
-provided.
+SH-degree schedule run as in the reference.  ``method="2dgs"`` keeps every
+Gaussian a thin surfel (third scale clamped to ``two_d_thickness`` times the
+scene extent after each update and density event) and, with its lambdas set,
+adds the depth-variance and normal-consistency losses of a second, feature
+compositing pass (trainer.py:180-259).
 """
 
 from __future__ import annotations
@@ -30,7 +33,7 @@ from ..cameras import Camera
 from ..distributed import allreduce_gradients, world
 from ..losses import l1_dssim_loss
 from .model import GaussianModel
-from .render import _render_fused, side_streams
+from .render import _project, _render_fused, side_streams
 
 __all__ = ["TrainerConfig", "GaussianTrainer"]
 
@@ -54,6 +57,10 @@ class TrainerConfig:
     lambda_dssim: float = 0.2
     antialias: bool = False
     projection: str = "ewa"
+    lambda_2d_depth_variance: float = 0.0  # 2DGS: ray-depth variance penalty
+    lambda_2d_normal_consistency: float = 0.0  # 2DGS: rendered vs depth-map normals
+    geometry_min_alpha: float = 0.05  # 2DGS: pixels below this alpha are left out of the geometry losses
+    two_d_thickness: float = 1e-4  # 2DGS: surfel thickness as a fraction of the scene extent
     densify_from: int = 500
     densify_until: int = 15000
     densify_every: int = 100
@@ -78,9 +85,8 @@ class GaussianTrainer:
     def __init__(self, model: GaussianModel, config: TrainerConfig | None = None, scene_extent: float = 1.0):
         self.model = model
         self.config = config or TrainerConfig()
-        if self.config.method not in {"vanilla", "mcmc"}:
-            raise ValueError("TrainerConfig.method must be 'vanilla' or 'mcmc' in mlx3d_b200 (the 2DGS surfel "
-                             "method is not provided)")
+        if self.config.method not in {"vanilla", "mcmc", "2dgs"}:
+            raise ValueError("TrainerConfig.method must be 'vanilla', 'mcmc', or '2dgs'")
         if self.config.projection not in {"ewa", "ut"}:
             raise ValueError("TrainerConfig.projection must be 'ewa' or 'ut'")
         self.scene_extent = scene_extent
@@ -94,6 +100,7 @@ class GaussianTrainer:
         self._v = {k: torch.zeros_like(model.params[k]) for k in _GROUPS}
         self._lr_last = self._schedule(0)
         self._reset_grad_accum()
+        self._apply_method_constraints()
 
     # ----------------------------------------------------------- schedules
     def _schedule(self, k: int) -> dict[str, float]:
@@ -118,6 +125,67 @@ class GaussianTrainer:
         self.grad_count = torch.zeros((n,), dtype=torch.float32, device=dev)
 
     # ------------------------------------------------------------- pieces
+    def _apply_method_constraints(self) -> None:
+        """2DGS: keep every Gaussian a thin surfel (trainer.py:180-183)."""
+        if self.config.method == "2dgs":
+            self.model.apply_2dgs_constraints(self.config.two_d_thickness * max(float(self.scene_extent), 1e-8))
+
+    def _geometry_loss_2dgs(self, camera: Camera):
+        """2DGS geometry terms (trainer.py:186-259): a second compositing pass
+        of per-Gaussian features [depth, depth^2, normal (3)] (normal = the
+        local z axis, flipped towards the camera), normalised by alpha; the
+        ray-depth variance E[z^2] - E[z]^2 and 1 - |cos| between the rendered
+        normals and the normals of the depth map's unprojected points, both
+        averaged over pixels with alpha > geometry_min_alpha.  Returns
+        (loss or None, metrics)."""
+        from .projection import quat_to_rotmat
+        from .rasterize import rasterize_features
+        from .tiles import bin_gaussians
+
+        cfg = self.config
+        metrics = {"depth_variance": 0.0, "normal_consistency": 0.0}
+        if cfg.method != "2dgs" or (cfg.lambda_2d_depth_variance <= 0 and cfg.lambda_2d_normal_consistency <= 0):
+            return None, metrics
+        p = self.model.params
+        W, H = camera.width, camera.height
+        dev = p["means"].device
+        proj = _project(camera, p["means"], p["quats"], torch.exp(p["scales"]), cfg.projection, cfg.antialias)
+        opac = torch.sigmoid(p["opacities"]) * proj["compensation"]
+        ids, ranges, tx, ty = bin_gaussians(proj["means2d"], proj["radii"], proj["depths"], W, H)
+        depths = proj["depths"]
+        normals = quat_to_rotmat(p["quats"])[:, :, 2]
+        view = camera.camera_center.to(dev) - p["means"]
+        normals = normals / torch.clamp(torch.linalg.norm(normals, dim=-1, keepdim=True), min=1e-8)
+        normals = torch.where((normals * view).sum(-1, keepdim=True) < 0, -normals, normals)
+        feats = torch.cat([depths[:, None], (depths * depths)[:, None], normals], dim=1)
+        geom = rasterize_features(proj["means2d"], proj["conics"], feats, opac, ids, ranges, W, H, tx, ty,
+                                  normalize=True)
+        valid = (geom["alpha"] > cfg.geometry_min_alpha).float()
+        denom = torch.clamp(valid.sum(), min=1.0)
+        ed, ed2 = geom["features"][..., 0], geom["features"][..., 1]
+        loss = torch.zeros((), device=dev)
+        if cfg.lambda_2d_depth_variance > 0:
+            dv = (torch.clamp(ed2 - ed * ed, min=0.0) * valid).sum() / denom
+            metrics["depth_variance"] = dv.detach()
+            loss = loss + float(cfg.lambda_2d_depth_variance) * dv
+        if cfg.lambda_2d_normal_consistency > 0 and W > 1 and H > 1:
+            u = torch.arange(W, dtype=torch.float32, device=dev) + 0.5
+            v = torch.arange(H, dtype=torch.float32, device=dev) + 0.5
+            uu, vv = u[None, :].expand(H, W), v[:, None].expand(H, W)
+            pts = camera.unproject_points(torch.stack([uu, vv], dim=-1), ed)
+            tan_x = pts[:-1, 1:] - pts[:-1, :-1]
+            tan_y = pts[1:, :-1] - pts[:-1, :-1]
+            dn = torch.linalg.cross(tan_x, tan_y)
+            dn = dn / torch.clamp(torch.linalg.norm(dn, dim=-1, keepdim=True), min=1e-8)
+            rn = geom["features"][:-1, :-1, 2:5]
+            rn = rn / torch.clamp(torch.linalg.norm(rn, dim=-1, keepdim=True), min=1e-8)
+            valid4 = valid[:-1, :-1] * valid[:-1, 1:] * valid[1:, :-1] * valid[1:, 1:]
+            cos = (rn * dn).sum(-1)
+            nc = ((1.0 - cos.abs()) * valid4).sum() / torch.clamp(valid4.sum(), min=1.0)
+            metrics["normal_consistency"] = nc.detach()
+            loss = loss + float(cfg.lambda_2d_normal_consistency) * nc
+        return loss, metrics
+
     def _view_forward(self, camera: Camera, target: torch.Tensor, probe: torch.Tensor | None):
         """Render + loss of one view (graph kept for the backward)."""
         cfg = self.config
@@ -132,6 +200,10 @@ class GaussianTrainer:
                 sh_degree=self.model.active_sh_degree, background=bg, antialias=cfg.antialias,
                 flags=nat.GS_ACT_EXP_SCALES | nat.GS_ACT_SIGMOID_OPACITY, probe=probe)
         loss, _, _ = l1_dssim_loss(out["image"], target, cfg.lambda_dssim)
+        geom, metrics = self._geometry_loss_2dgs(camera)
+        if geom is not None:
+            loss = loss + geom
+        self._geometry = metrics
         return loss, out
 
     def _view_loss(self, camera: Camera, target: torch.Tensor, probe: torch.Tensor | None, scale: float):
@@ -222,7 +294,8 @@ class GaussianTrainer:
         return {"loss": loss, "num_gaussians": self.model.num_gaussians, "step": self.step_count,
                 "active_sh_degree": self.model.active_sh_degree, "lr_means": self.learning_rates()["means"],
                 "method": self.config.method, "densify": densify, "opacity_reset": opacity_reset,
-                "sh_degree_changed": sh_changed, "geometry": {}}
+                "sh_degree_changed": sh_changed,
+                "geometry": {k: float(v) for k, v in getattr(self, "_geometry", {}).items()}}
 
     # --------------------------------------------------------------- steps
     def step(self, camera: Camera, target: torch.Tensor) -> dict:
@@ -233,6 +306,7 @@ class GaussianTrainer:
         loss, out = self._view_loss(camera, target, probe, 1.0)
         self._adam()
         self._mcmc_noise()
+        self._apply_method_constraints()
         densify = None
         if track:
             with torch.no_grad():
@@ -242,6 +316,7 @@ class GaussianTrainer:
                 self.grad_count += visible
             if self.step_count % cfg.densify_every == 0 and self.step_count > cfg.densify_from:
                 densify = self._density_event()
+                self._apply_method_constraints()
         opacity_reset, sh_changed = self._schedules_after_update()
         return self._info(float(loss), opacity_reset, sh_changed, densify)
 
@@ -306,6 +381,7 @@ class GaussianTrainer:
         allreduce_gradients({k: self.model.params[k] for k in _GROUPS})
         self._adam()
         self._mcmc_noise()
+        self._apply_method_constraints()
         opacity_reset, sh_changed = self._schedules_after_update()
         info = self._info(float(loss_sum) / max(len(cameras), 1), opacity_reset, sh_changed)
         info["views"] = len(cameras)

@@ -13,6 +13,9 @@ differentiation (the reference gets these gradients from MLX autodiff):
   trainer's loss, trainer.py:300-305 (depthwise conv2d, zero padding).
 * ``adam_update`` — mlx.optimizers.Adam.apply_single as the trainer builds it
   (trainer.py:128), float32 numpy, one rounding per operation.
+* ``geometry_loss_2dgs`` — the 2DGS geometry terms, trainer.py:186-259, on the
+  naive renderer's feature composite (cameras.py:327-336 for the unprojection,
+  pinhole cameras).
 
 The product package never imports this module.
 """
@@ -123,10 +126,11 @@ def view_dirs(camera, means):
 
 
 def naive_render(camera, means, quats, scales, opacities, colors, background=None, antialias=False):
-    """reference.py:16-74: every Gaussian at every pixel, global depth order."""
+    """reference.py:16-74: every Gaussian at every pixel, global depth order
+    (``colors`` may have any number C of channels; background (C,))."""
     dt = means.dtype
     if background is None:
-        background = torch.zeros(3, dtype=dt)
+        background = torch.zeros(colors.shape[1], dtype=dt)
     H, W = camera.height, camera.width
     proj = project(camera, means, quats, scales, antialias=antialias)
     order = torch.argsort(proj["depths"].detach(), stable=True)
@@ -251,3 +255,45 @@ def project_ut(camera, means, quats, scales, blur=0.3, antialias=False):
     valid = (zc > camera.znear) & (det > 0)
     return {"means2d": m2, "conics": conics, "depths": zc, "radii": torch.where(valid, radii, 0 * radii).detach(),
             "compensation": torch.where(valid, comp, 0 * comp)}
+
+
+def geometry_loss_2dgs(camera, means, quats, scales, opacities, antialias=False, lam_var=0.0, lam_normal=0.0,
+                       min_alpha=0.05):
+    """(loss, depth_variance, normal_consistency) of trainer.py:186-259 with
+    ``opacities`` activated; features [z, z^2, normal] composited by the naive
+    renderer and normalised by alpha (rasterize.py:535-544)."""
+    dt = means.dtype
+    proj = project(camera, means, quats, scales, antialias=antialias)
+    q = quats / torch.linalg.norm(quats, dim=-1, keepdim=True)
+    w, x, y, z = q.unbind(-1)
+    normals = torch.stack([2 * (x * z + w * y), 2 * (y * z - w * x), 1 - 2 * (x * x + y * y)], -1)
+    center = (-(camera.R.T.to(torch.float32) @ camera.t.to(torch.float32))).to(dt)
+    view = center - means
+    normals = normals / torch.clamp(torch.linalg.norm(normals, dim=-1, keepdim=True), min=1e-8)
+    normals = torch.where((normals * view).sum(-1, keepdim=True) < 0, -normals, normals)
+    d = proj["depths"]
+    feats = torch.cat([d[:, None], (d * d)[:, None], normals], 1)
+    out = naive_render(camera, means, quats, scales, opacities, feats, antialias=antialias)
+    alpha = out["alpha"]
+    a = alpha[..., None]
+    f = torch.where(a > 1e-6, out["image"] / torch.clamp(a, min=1e-6), torch.zeros_like(out["image"]))
+    valid = (alpha > min_alpha).to(dt)
+    denom = torch.clamp(valid.sum(), min=1.0)
+    ed, ed2 = f[..., 0], f[..., 1]
+    dv = (torch.clamp(ed2 - ed * ed, min=0.0) * valid).sum() / denom
+    H, W = camera.height, camera.width
+    u = torch.arange(W, dtype=dt) + 0.5
+    v = torch.arange(H, dtype=dt) + 0.5
+    xd = (u[None, :].expand(H, W) - camera.cx) / camera.fx
+    yd = (v[:, None].expand(H, W) - camera.cy) / camera.fy
+    pc = torch.stack([xd * ed, yd * ed, ed], -1)
+    pts = (pc - camera.t.to(dt)) @ camera.R.to(dt)
+    tx = pts[:-1, 1:] - pts[:-1, :-1]
+    ty = pts[1:, :-1] - pts[:-1, :-1]
+    dn = torch.linalg.cross(tx, ty)
+    dn = dn / torch.clamp(torch.linalg.norm(dn, dim=-1, keepdim=True), min=1e-8)
+    rn = f[:-1, :-1, 2:5]
+    rn = rn / torch.clamp(torch.linalg.norm(rn, dim=-1, keepdim=True), min=1e-8)
+    valid4 = valid[:-1, :-1] * valid[:-1, 1:] * valid[1:, :-1] * valid[1:, 1:]
+    nc = ((1.0 - (rn * dn).sum(-1).abs()) * valid4).sum() / torch.clamp(valid4.sum(), min=1.0)
+    return lam_var * dv + lam_normal * nc, dv, nc
