@@ -276,12 +276,15 @@ def run_ours(args, world, rank, local):
         step()
     drain()
     torch.cuda.synchronize()
-    barrier()
-    torch.cuda.synchronize()
     lib = nat.load()
-    launches0 = lib.gs_kernel_launch_count()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # The clock sampler starts (NVML set-up takes a while, and differs per
+    # process) before the barrier, so every rank records its start event
+    # right after the same barrier.
     with ClockSampler(local) as clocks:
+        barrier()
+        torch.cuda.synchronize()
+        launches0 = lib.gs_kernel_launch_count()
         start.record()
         for _ in range(args.steps):
             step()
@@ -641,12 +644,13 @@ def run_multiview(args, world, rank, local, config=None, steps=None, warmup=None
     for _ in range(warmup):
         step()
     torch.cuda.synchronize()
-    barrier()
     dups.clear()
     lib = nat.load()
-    l0 = lib.gs_kernel_launch_count()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with ClockSampler(local) as clocks:
+    with ClockSampler(local) as clocks:  # started before the barrier (see run_ours)
+        barrier()
+        torch.cuda.synchronize()
+        l0 = lib.gs_kernel_launch_count()
         e0.record()
         for _ in range(steps):
             step()
