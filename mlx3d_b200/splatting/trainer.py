@@ -30,7 +30,7 @@ import torch
 
 from .. import _native as nat
 from ..cameras import Camera
-from ..distributed import allreduce_gradients, world
+from ..distributed import GradientReducer, world
 from ..losses import l1_dssim_loss
 from .model import GaussianModel
 from .render import _project, _render_fused, side_streams
@@ -320,7 +320,7 @@ class GaussianTrainer:
         opacity_reset, sh_changed = self._schedules_after_update()
         return self._info(float(loss), opacity_reset, sh_changed, densify)
 
-    def _views_backward(self, cameras, targets, scale: float, streams: int) -> list:
+    def _views_backward(self, cameras, targets, scale: float, streams: int, first_sink=None) -> list:
         """Forward + backward of every view, gradients accumulated in .grad.
 
         With ``streams`` > 1 the views are pipelined: view i's forward runs
@@ -329,9 +329,21 @@ class GaussianTrainer:
         overlap the compositor backward of the other.  Every backward waits
         for the previous view's backward (an event), so the accumulations
         into .grad stay ordered; the current stream waits for all of them.
-        Returns the detached per-view losses (usable on the current stream)."""
+        ``first_sink`` (a context manager) is entered around the first view's
+        backward (the one that creates .grad).  Returns the detached per-view
+        losses (usable on the current stream)."""
+        import contextlib
+
+        sink = first_sink if first_sink is not None else contextlib.nullcontext()
         if streams <= 1 or len(cameras) <= 1:
-            return [self._view_loss(c, t, None, scale)[0] for c, t in zip(cameras, targets)]
+            out = []
+            for i, (c, t) in enumerate(zip(cameras, targets)):
+                if i == 0:
+                    with sink:
+                        out.append(self._view_loss(c, t, None, scale)[0])
+                else:
+                    out.append(self._view_loss(c, t, None, scale)[0])
+            return out
         cur = torch.cuda.current_stream()
         ss = side_streams(streams)
         for s in ss:
@@ -342,10 +354,10 @@ class GaussianTrainer:
             with torch.cuda.stream(s):
                 loss, _ = self._view_forward(cam, tgt, None)
             if pending is not None:  # previous view's backward, issued after this view's forward
-                prev_bwd = self._issue_backward(*pending, prev_bwd)
+                prev_bwd = self._issue_backward(*pending, prev_bwd, sink if i == 1 else None)
             pending = (loss, scale, s)
             losses.append(loss.detach())
-        self._issue_backward(*pending, prev_bwd)
+        self._issue_backward(*pending, prev_bwd, sink if len(cameras) == 1 else None)
         for s in ss:
             cur.wait_stream(s)
         for loss in losses:  # made on the side streams, read on the current one
@@ -353,8 +365,10 @@ class GaussianTrainer:
         return losses
 
     @staticmethod
-    def _issue_backward(loss, scale, s, after):
-        with torch.cuda.stream(s):
+    def _issue_backward(loss, scale, s, after, sink=None):
+        import contextlib
+
+        with torch.cuda.stream(s), (sink if sink is not None else contextlib.nullcontext()):
             if after is not None:
                 s.wait_event(after)
             (loss * scale).backward()
@@ -376,9 +390,27 @@ class GaussianTrainer:
         rank, ws = world()
         if total_views is None:
             total_views = len(cameras) * ws
-        losses = self._views_backward(cameras, targets, 1.0 / total_views, streams)
+        plist = [self.model.params[k] for k in _GROUPS]
+        red = None
+        if ws > 1:
+            # the first view's backward writes the gradients straight into the
+            # flat all-reduce buffer (later views accumulate into them in
+            # place), so the all-reduce needs no gathering copy
+            if getattr(self, "_reducer", None) is None:
+                self._reducer = GradientReducer()
+            red = self._reducer
+            for p in plist:
+                p.grad = None
+        losses = self._views_backward(cameras, targets, 1.0 / total_views, streams,
+                                      first_sink=red.sink(plist) if red is not None else None)
         loss_sum = torch.stack(losses).sum() if losses else torch.zeros((), device=self.model.params["means"].device)
-        allreduce_gradients({k: self.model.params[k] for k in _GROUPS})
+        if red is not None:
+            red.stage(plist)  # copies only gradients that did not land in the buffer
+            flat = red.finish()  # the all-reduce, waited for on the current stream
+            off = 0
+            for p in plist:
+                p.grad = flat[off:off + p.numel()].view_as(p)
+                off += p.numel()
         self._adam()
         self._mcmc_noise()
         self._apply_method_constraints()

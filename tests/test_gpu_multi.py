@@ -93,3 +93,59 @@ def test_two_gpu_exchanges_match_allreduce():
         for r in (0, 1):
             for key, err in results[r].items():
                 assert err < 1e-5, (r, key, err)
+
+
+def _trainer_worker(rank, port, results):
+    import torch.distributed as dist
+
+    from mlx3d_b200.distributed import shard_views
+    from mlx3d_b200.scenes import make_scene
+    from mlx3d_b200.splatting import GaussianModel, GaussianTrainer, TrainerConfig
+    from tests.helpers import rel_l2
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=2, device_id=torch.device("cuda", rank))
+    try:
+        sc = make_scene(3, n=40_000, views=5)
+        cams = sc.cameras
+        targets = [sc.target(i, device="cuda") for i in range(len(cams))]
+
+        def trainer():
+            m = GaussianModel({k: v.clone() for k, v in sc.torch_params(device="cuda").items()}, sh_degree=3)
+            m.active_sh_degree = 3
+            t = GaussianTrainer(m, TrainerConfig(densify_from=10**9))
+            seen = {}
+            t._adam = lambda: seen.update({k: p.grad.clone() for k, p in m.params.items()})
+            return t, seen
+
+        tr, got = trainer()
+        mine = shard_views(list(range(len(cams))), rank, 2)
+        tr.step_views([cams[i] for i in mine], [targets[i] for i in mine], total_views=len(cams))
+        ref, _ = trainer()
+        ref._views_backward(cams, targets, 1.0 / len(cams), 2)  # all views on this rank, no collective
+        results[rank] = {k: rel_l2(got[k].cpu().numpy(), p.grad.cpu().numpy()) for k, p in ref.model.params.items()}
+    finally:
+        dist.destroy_process_group()
+
+
+@needs_two
+def test_two_gpu_training_step_gradients_equal_all_views_on_one_gpu():
+    """GaussianTrainer.step_views on 2 ranks (gradients written straight into
+    the flat all-reduce buffer, all-reduced over NCCL) equals the gradient of
+    all views accumulated on one GPU."""
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as m:
+        results = m.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_trainer_worker, args=(r, port, results)) for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=300)
+            assert p.exitcode == 0
+        for r in (0, 1):
+            for k, err in results[r].items():
+                assert err < 1e-5, (r, k, err)
