@@ -159,6 +159,27 @@ class GradientReducer:
                 entry[0] = (dist.all_reduce(entry[1], op=dist.ReduceOp.SUM, group=self.group, async_op=True)
                             if ws > 1 else True)
 
+    def launch_chunks(self, n_chunks: int) -> tuple[torch.Tensor, list]:
+        """Take the oldest staged buffer (not launched yet) and launch its
+        all-reduce as ``n_chunks`` separate asynchronous calls, so a consumer
+        can start on the first chunk's sum while the later ones are still
+        being reduced.  Returns (buffer, [(begin, end, work or None)]) in
+        element offsets; the caller waits for each work (``work.wait()``
+        makes the current stream wait) before reading that chunk."""
+        if not self._pending or self._pending[0][0] is not None:
+            raise RuntimeError("GradientReducer.launch_chunks: nothing staged")
+        _, buf = self._pending.pop(0)
+        _, ws = world()
+        n = buf.numel()
+        step = max(64, ((-(-n // max(1, n_chunks))) + 63) // 64 * 64)
+        chunks = []
+        for a in range(0, n, step):
+            b = min(n, a + step)
+            w = (dist.all_reduce(buf[a:b], op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+                 if ws > 1 else None)
+            chunks.append((a, b, w))
+        return buf, chunks
+
     def start(self, params: dict[str, torch.Tensor] | list[torch.Tensor]) -> None:
         """stage + launch."""
         self.stage(params)

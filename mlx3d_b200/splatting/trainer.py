@@ -211,6 +211,41 @@ class GaussianTrainer:
         (loss * scale).backward()
         return loss.detach(), out
 
+    def _adam_chunked(self, flat: torch.Tensor, chunks: list) -> None:
+        """The Adam update of a step whose gradients are the flat buffer
+        ``flat`` (parameter order _GROUPS) being all-reduced in ``chunks``
+        ((begin, end, work) element ranges): each chunk's parameter rows are
+        updated as soon as its sum has arrived, while the later chunks are
+        still on the wire (one launch per chunk over the parameters it
+        intersects)."""
+        self.step_count += 1
+        lrs = self._schedule(self.step_count - 1)
+        self._lr_last = lrs
+        c = self.config
+        spans, off = [], 0
+        for k in _GROUPS:
+            n = self.model.params[k].numel()
+            spans.append((k, off, off + n))
+            off += n
+        for a, b, work in chunks:
+            if work is not None:
+                work.wait()
+            groups = (nat.GsAdamGroup * len(_GROUPS))()
+            ng = 0
+            for k, lo, hi in spans:
+                s0, s1 = max(a, lo), min(b, hi)
+                if s0 >= s1:
+                    continue
+                p, d = self.model.params[k], s0 - lo
+                groups[ng] = nat.GsAdamGroup(p.data_ptr() + 4 * d, flat.data_ptr() + 4 * s0,
+                                             self._m[k].data_ptr() + 4 * d, self._v[k].data_ptr() + 4 * d,
+                                             s1 - s0, lrs[k])
+                ng += 1
+            nat.call("gs_adam_step", groups, ng, c.adam_betas[0], c.adam_betas[1], c.adam_eps,
+                     int(c.adam_bias_correction), self.step_count, nat.stream())
+        for k in _GROUPS:
+            self.model.params[k].grad = None
+
     def _adam(self) -> None:
         self.step_count += 1
         lrs = self._schedule(self.step_count - 1)
@@ -406,12 +441,10 @@ class GaussianTrainer:
         loss_sum = torch.stack(losses).sum() if losses else torch.zeros((), device=self.model.params["means"].device)
         if red is not None:
             red.stage(plist)  # copies only gradients that did not land in the buffer
-            flat = red.finish()  # the all-reduce, waited for on the current stream
-            off = 0
-            for p in plist:
-                p.grad = flat[off:off + p.numel()].view_as(p)
-                off += p.numel()
-        self._adam()
+            flat, chunks = red.launch_chunks(4)  # the all-reduce, in four asynchronous pieces
+            self._adam_chunked(flat, chunks)  # each piece's rows updated once its sum arrived
+        else:
+            self._adam()
         self._mcmc_noise()
         self._apply_method_constraints()
         opacity_reset, sh_changed = self._schedules_after_update()

@@ -118,7 +118,18 @@ def _trainer_worker(rank, port, results):
             m.active_sh_degree = 3
             t = GaussianTrainer(m, TrainerConfig(densify_from=10**9))
             seen = {}
-            t._adam = lambda: seen.update({k: p.grad.clone() for k, p in m.params.items()})
+
+            def record(flat, chunks):  # the summed gradient, instead of the update
+                for _, _, w in chunks:
+                    if w is not None:
+                        w.wait()
+                off = 0
+                for k in ("means", "scales", "quats", "opacities", "sh_dc", "sh_rest"):
+                    n = m.params[k].numel()
+                    seen[k] = flat[off:off + n].view_as(m.params[k]).clone()
+                    off += n
+
+            t._adam_chunked = record
             return t, seen
 
         tr, got = trainer()
