@@ -2,9 +2,20 @@
 
 Views are independent until the per-Gaussian gradient sum, so a multi-view
 render or training step shards the views over ranks (view k goes to rank
-k mod world) and sums the gradients of the replicated Gaussian parameters
-with one all-reduce per parameter tensor — the only collective on this path.
-The reference has no multi-device code; this is the B200 build's addition.
+k mod world) and sums the gradients of the replicated Gaussian parameters.
+Two ways of summing:
+
+* all-reduce of the flat parameter gradients (``allreduce_gradients``,
+  ``GradientReducer``: asynchronous, optionally in chunks, gradients written
+  straight into the flat buffer) — what a replicated optimizer needs;
+* exchange of the 9 screen-space cotangent floats per Gaussian instead of
+  the 59 gradient floats, each rank reducing its slice of the Gaussians over
+  every rank's views (``ScreenGradientExchange`` over an NCCL all-to-all,
+  ``PeerScreenExchange`` over peer memory read directly through NVLink) —
+  the gradient ends reduce-scattered.
+
+``PeerMonitor`` lets ranks notice between steps that one of them left.  The
+reference has no multi-device code; this is the B200 build's addition.
 """
 
 from __future__ import annotations
